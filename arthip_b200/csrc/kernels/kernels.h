@@ -1,0 +1,116 @@
+// Host-side launch interface of the device kernels (sm_100a).
+//
+// Tensors are fp16 NHWC ([H][W][C], batch 1) inside the engine; the graph boundary is
+// NCHW in the model's IO dtype. Every launcher returns a cudaError_t from the launch.
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+#include <string>
+#include <vector>
+
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+namespace ah {
+
+enum Act : int { kActNone = 0, kActRelu = 1, kActSilu = 2 };
+
+// ---------------------------------------------------------------------------
+// tcgen05 implicit-GEMM 3x3 convolution (conv_tc.cu)
+// ---------------------------------------------------------------------------
+constexpr int kTcMaxChunks = 4;   // input channels <= 256
+constexpr int kTcTilePx = 128;    // output pixels per MMA tile (one row segment)
+constexpr int kTcBoxPx = 130;     // input pixels staged per row (tile + 1-pixel halo each side)
+
+struct ConvTcChunk {
+  int c0 = 0;        // first input channel of the chunk
+  int cw = 0;        // channels in the chunk: 64, 32 or 16
+  int rowbytes = 0;  // cw * 2 (one pixel row of the K-major operand)
+  int layout = 0;    // smem descriptor layout code: 2 = 128B swizzle, 4 = 64B, 6 = 32B
+  int area = 0;      // bytes of this chunk inside one input-row slot (1024-aligned)
+  int slot_off = 0;  // offset of this chunk inside a slot
+};
+
+// Everything the kernel needs that depends only on (C, M, weights): built once per model.
+struct ConvTcWeights {
+  int C = 0, M = 0;
+  int nchunks = 0;
+  ConvTcChunk chunk[kTcMaxChunks];
+  void* wpack = nullptr;       // device: [tap][chunk] blocks of M swizzled rows
+  size_t wpack_bytes = 0;
+  long long gofs[9 * kTcMaxChunks] = {};  // byte offset of each (tap, chunk) block
+  float* bias = nullptr;       // device: M fp32 (fp16-rounded values)
+};
+
+// Per (layer, input buffer, frame size) launch plan.
+struct ConvTcPlan {
+  const ConvTcWeights* w = nullptr;
+  int H = 0, W = 0;
+  int MT = 0, n_msplit = 1;    // output channels per CTA and number of channel slices
+  int nslots = 0;
+  int slot_bytes = 0;
+  int wofs[9 * kTcMaxChunks] = {};  // smem offset of each (tap, chunk) weight block
+  int w_smem_bytes = 0;
+  size_t smem_bytes = 0;
+  int nacc = 0, acc_stride = 0, tmem_cols = 0;
+  int grid_x = 0;
+  CUtensorMap maps[kTcMaxChunks];
+};
+
+// Returns true when the tensor-core kernel covers (C, M); otherwise fills `why`.
+bool conv_tc_supported(int C, int M, std::string* why);
+// Packs fp16 weights OIHW [M][C][3][3] (host, as fp16 bits) and fp32 bias into device memory.
+cudaError_t conv_tc_upload(const uint16_t* w_oihw_f16, const float* bias_or_null, int C, int M,
+                           ConvTcWeights* out);
+void conv_tc_free(ConvTcWeights* w);
+// Host-only packing (exposed for tests): returns the packed byte image.
+std::vector<uint8_t> conv_tc_pack_host(const uint16_t* w_oihw_f16, int C, int M, ConvTcWeights* layout);
+// Builds the per-frame plan (tensor maps over `in`). Fails with a message when smem cannot fit.
+bool conv_tc_plan(const ConvTcWeights* w, const __half* in, int H, int W, int num_sms, ConvTcPlan* plan,
+                  std::string* err);
+cudaError_t conv_tc_launch(const ConvTcPlan& plan, const __half* add1, const __half* add2, __half* out,
+                           int act, uint32_t* status, cudaStream_t stream, int desc_base_mode = 1);
+
+// ---------------------------------------------------------------------------
+// CUDA-core convolution for narrow layers (conv_simt.cu): C==1 heads, small M
+// tails (with fused DepthToSpace / Clip / boundary layout), odd channel counts.
+// ---------------------------------------------------------------------------
+struct SimtOut {
+  void* ptr = nullptr;
+  int dts_b = 1;        // DepthToSpace block size (1 = none); DCR channel order
+  int nchw = 0;         // 1: write [Cout][H*b][W*b] (graph boundary), 0: NHWC
+  int fp32 = 0;         // 1: fp32 elements
+  int clip = 0;
+  float clip_lo = 0.f, clip_hi = 0.f;
+};
+
+struct SimtConvWeights {
+  int C = 0, M = 0;
+  float* w = nullptr;    // device: [tap][c][m] fp32 (values of the fp16 weights)
+  float* bias = nullptr; // device: M fp32
+};
+cudaError_t simt_conv_upload(const uint16_t* w_oihw_f16, const float* bias_or_null, int C, int M,
+                             SimtConvWeights* out);
+void simt_conv_free(SimtConvWeights* w);
+cudaError_t simt_conv_launch(const SimtConvWeights& w, const __half* in, int H, int W, const __half* add1,
+                             const __half* add2, int act, const SimtOut& out, cudaStream_t stream);
+
+// ---------------------------------------------------------------------------
+// Pointwise / layout kernels (pointwise.cu)
+// ---------------------------------------------------------------------------
+enum UnaryOp : int { kSigmoid = 0, kClip = 1, kRelu = 2 };
+cudaError_t unary_launch(const __half* in, __half* out, size_t n, int op, float lo, float hi,
+                         cudaStream_t s);
+enum BinaryOp : int { kAdd = 0, kMul = 1 };
+cudaError_t binary_launch(const __half* a, const __half* b, __half* out, size_t n, int op, cudaStream_t s);
+// NHWC [H][W][Cout*b*b] -> DepthToSpace (DCR) -> SimtOut layout, optional clip.
+cudaError_t dts_launch(const __half* in, int H, int W, int Cin, const SimtOut& out, cudaStream_t s);
+// Boundary layout conversions. NCHW (fp16|fp32) -> NHWC fp16, and back.
+cudaError_t nchw_to_nhwc_launch(const void* in, int in_fp32, __half* out, int C, int H, int W,
+                                cudaStream_t s);
+cudaError_t nhwc_to_nchw_launch(const __half* in, void* out, int out_fp32, int C, int H, int W,
+                                cudaStream_t s);
+
+}  // namespace ah

@@ -1,0 +1,133 @@
+/* arthip_b200 — C ABI of the B200-native fp16 conv-chain engine.
+ *
+ * All functions are plain C: pointers, sizes and ints only. Return codes follow the
+ * reference's engine driver (tests/correctness/harness/engine_harness.cc:12-15):
+ *   0 = ok, 1 = build / shape / argument failure, 2 = run failure.
+ * Error text is copied (NUL-terminated, truncated) into the caller's `err` buffer.
+ * Host IO buffers are NCHW plane-major in the model's IO dtype (fp16, or fp32 for
+ * models with fp32 boundary Casts), exactly like vship::HipEngine::Run
+ * (src/vapoursynth/hip_engine.h:100-105).
+ */
+#ifndef ARTHIP_B200_H
+#define ARTHIP_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ------------------------------------------------------------------------------
+ * Reference engine-driver ABI (drop-in for tests/correctness/harness/engine_harness.cc)
+ * ---------------------------------------------------------------------------- */
+
+/* Replaces engine_device_count (engine_harness.cc:56-63). */
+int engine_device_count(int* count);
+
+/* Replaces engine_probe (engine_harness.cc:65-94): build `model_path` on `device`,
+ * report IO dtypes, the first conv's input channels / last conv's output channels and
+ * the NCHW output shape for input [N, C, H, W]. */
+int engine_probe(const char* model_path, int N, int H, int W, int C, int device, char* err, int errlen,
+                 int* in_fp32, int* out_fp32, int* cin, int* cout, int64_t* out_shape, int* out_rank);
+
+/* Replaces engine_run (engine_harness.cc:96-145): one frame through a fresh engine. */
+int engine_run(const char* model_path, int N, int H, int W, int C, int device, const void* input,
+               size_t input_bytes, void* out, size_t cap, size_t* out_bytes, int* out_fp32, int64_t* out_shape,
+               int* out_rank, char* err, int errlen);
+
+/* Replaces engine_alloc_failure_then_run (engine_harness.cc:151-210): an oversized frame
+ * must fail with the allocation error and the same engine must then run a 16x16 frame. */
+int engine_alloc_failure_then_run(const char* model_path, int N, int bigH, int bigW, int C, int device,
+                                  const void* recovery_input, size_t recovery_input_bytes, void* out, size_t cap,
+                                  size_t* out_bytes, int* out_fp32, int64_t* out_shape, int* out_rank,
+                                  char* failerr, int failerrlen, char* runerr, int runerrlen);
+
+/* ------------------------------------------------------------------------------
+ * Persistent engine handle. Replaces the vship::HipEngine C++ object the VapourSynth
+ * plugin holds per stream (src/vapoursynth/vs_hip.cpp:517-527, hip_engine.h:88-131) and
+ * the hip::HipGraph the ORT EP compiles per partition (src/onnxruntime-hip/hip_graph.h:91-167).
+ * ---------------------------------------------------------------------------- */
+typedef struct ah_engine ah_engine;
+
+/* HipEngine(int device_id) + Build(ModelProto) from a file or serialized bytes. */
+int ah_engine_create_from_file(const char* model_path, int device, ah_engine** out, char* err, int errlen);
+int ah_engine_create_from_bytes(const void* model, size_t model_bytes, int device, ah_engine** out, char* err,
+                                int errlen);
+void ah_engine_destroy(ah_engine* e);
+
+/* InputIsFp32 / OutputIsFp32 / InputChannels / OutputChannels (hip_engine.h:118-131). */
+int ah_engine_info(ah_engine* e, int* in_fp32, int* out_fp32, int* cin, int* cout);
+
+/* GetOutputShape (hip_engine.h:96-98): NCHW in, NCHW out (4 values). */
+int ah_engine_output_shape(ah_engine* e, int N, int C, int H, int W, int64_t* out_shape4);
+
+/* Run (hip_engine.h:104-105): host NCHW input/output, synchronous, thread-safe.
+ * Pinned (page-locked) host buffers are transferred directly; pageable ones through the
+ * engine's pinned staging. */
+int ah_engine_run(ah_engine* e, int N, int C, int H, int W, const void* input, size_t input_bytes, void* output,
+                  size_t output_cap, char* err, int errlen);
+
+/* Device-resident frames: build the plan for [N,C,H,W] and return the engine's device
+ * boundary buffers (NCHW, model IO dtype; valid until the next shape change). */
+int ah_engine_prepare(ah_engine* e, int N, int C, int H, int W, void** in_dev, void** out_dev, size_t* in_bytes,
+                      size_t* out_bytes, char* err, int errlen);
+/* Enqueue one frame (input buffer -> output buffer) on the engine's stream; asynchronous.
+ * Replays a CUDA graph captured per resolution. */
+int ah_engine_enqueue(ah_engine* e, char* err, int errlen);
+int ah_engine_synchronize(ah_engine* e, char* err, int errlen);
+/* The engine's CUDA stream (cudaStream_t) for ordering caller copies with frames. */
+void* ah_engine_stream(ah_engine* e);
+
+/* Per-op timing over up to max_frames enqueued frames (CUDA events on the engine
+ * stream); read returns per-op summed ms (n_ops entries) and the first-to-last span. */
+int ah_engine_timing_start(ah_engine* e, int max_frames, char* err, int errlen);
+int ah_engine_timing_read(ah_engine* e, double* op_ms, int n_ops, double* span_ms, int* frames, char* err,
+                          int errlen);
+/* Device op list of the prepared plan: kernel family, label, algorithmic FLOPs and bytes. */
+int ah_engine_num_ops(ah_engine* e);
+int ah_engine_op_info(ah_engine* e, int i, char* kind, int kindlen, char* label, int labellen, double* flops,
+                      double* bytes);
+/* Fused op list (one line per op), for inspection. */
+int ah_engine_describe(ah_engine* e, char* buf, int len);
+
+/* Parse + fuse a model without touching any GPU (fusion decisions / rejections). */
+int ah_model_inspect(const char* model_path, char* buf, int len, int* in_fp32, int* out_fp32, int* cin,
+                     int* cout, char* err, int errlen);
+
+/* ------------------------------------------------------------------------------
+ * Single fused conv layer (3x3, stride 1, pad 1) on device NHWC fp16 tensors:
+ * out = [add2 +] [add1 +] act(conv(in, w) + bias). Replaces one winograd_conv /
+ * direct_conv dispatch (src/common/hip_kernels.h:143-483) as the engine issues it.
+ * ---------------------------------------------------------------------------- */
+typedef struct ah_conv ah_conv;
+
+/* w_oihw_f16: [M][C][3][3] fp16 bit patterns (host); bias: M floats or NULL;
+ * act: 0 none, 1 ReLU, 2 SiLU. */
+int ah_conv3x3_create(int device, int C, int M, const uint16_t* w_oihw_f16, const float* bias, int act,
+                      ah_conv** out, char* err, int errlen);
+/* Enqueue on `stream` (cudaStream_t, NULL = legacy default). add1/add2 may be NULL. */
+int ah_conv3x3_run(ah_conv* c, const void* in_nhwc, int H, int W, const void* add1, const void* add2,
+                   void* out_nhwc, void* stream, char* err, int errlen);
+/* 0 = tcgen05 tensor-core kernel, 1 = CUDA-core kernel. */
+int ah_conv3x3_kind(ah_conv* c);
+/* Reads and clears the device error word the tensor-core kernel writes on a timed-out
+ * pipeline wait (0 = none). Synchronises the device. */
+int ah_conv3x3_status(ah_conv* c, uint32_t* status);
+void ah_conv3x3_destroy(ah_conv* c);
+
+/* ------------------------------------------------------------------------------
+ * Host fp16 conversions used at load time (no GPU).
+ * RNE: hip_engine.cc:1190-1232 (FloatToHalfBitsRNE). FTZ: convert_float_to_float16.cpp:165-186.
+ * ---------------------------------------------------------------------------- */
+void ah_float_to_half_rne(const float* in, uint16_t* out, size_t n);
+void ah_float_to_half_ftz(const float* in, uint16_t* out, size_t n);
+void ah_half_to_float(const uint16_t* in, float* out, size_t n);
+
+const char* ah_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ARTHIP_B200_H */

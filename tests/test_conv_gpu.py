@@ -1,0 +1,100 @@
+"""Single fused conv layers on the GPU against an fp32 cuDNN reference of the same layer.
+
+Covers the tcgen05 tensor-core kernel (every supported channel-chunk combination,
+partial column strips, 1-row frames, channel-sliced launches, fused ReLU/SiLU and one or
+two residual adds) and the CUDA-core kernel (C==1 heads, narrow tails, odd widths).
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from gpu_util import assert_fp16_layer_close, torch_conv_layer
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+
+def _case(C, M, H, W, act, nadds, seed):
+    from arthip_b200.engine import Conv3x3
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    dev = torch.device("cuda:0")
+    x = torch.rand(1, H, W, C, generator=g).half().to(dev)
+    w = (torch.randn(M, C, 3, 3, generator=g) * (2.0 / (9 * C)) ** 0.5).numpy().astype(np.float16)
+    b = (torch.randn(M, generator=g) * 0.05).numpy().astype(np.float16)
+    adds = [torch.randn(1, H, W, M, generator=g).half().to(dev) for _ in range(nadds)]
+    out = torch.full((1, H, W, M), float("nan"), dtype=torch.float16, device=dev)
+    conv = Conv3x3(w, b.astype(np.float32), act=act)
+    conv.run(x.data_ptr(), H, W, out.data_ptr(), *(a.data_ptr() for a in adds),
+             stream=torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    assert conv.status() == 0, "kernel reported a pipeline timeout"
+    ref = torch_conv_layer(x, w, b, act, adds)
+    return conv.kind, out.float().cpu().numpy(), ref.cpu().numpy()
+
+
+TC_CASES = [
+    # C, M, H, W, act, nadds
+    (64, 64, 37, 300, 1, 0),     # 3 strips, last partial
+    (64, 64, 9, 128, 0, 1),      # exactly one strip, residual add
+    (64, 64, 5, 131, 1, 2),      # block conv with residual + global skip
+    (64, 64, 1, 5, 1, 0),        # a single short row
+    (64, 64, 64, 64, 2, 0),      # SiLU epilogue
+    (32, 32, 33, 129, 1, 1),     # 64B-swizzle chunk
+    (16, 16, 17, 200, 0, 0),     # 32B-swizzle chunk
+    (48, 80, 11, 140, 1, 0),     # chunks 32+16, N=80
+    (96, 96, 13, 150, 1, 1),     # chunks 64+32 (R16F96 layers)
+    (128, 128, 8, 140, 1, 0),    # two 64-chunks; channel-sliced launch
+    (64, 256, 6, 130, 0, 0),     # N split across CTAs
+    (128, 16, 4, 129, 0, 0),     # two chunks, narrow N
+]
+
+
+@pytest.mark.parametrize("C,M,H,W,act,nadds", TC_CASES)
+def test_tensor_core_conv_matches_fp32_reference(C, M, H, W, act, nadds):
+    kind, got, ref = _case(C, M, H, W, act, nadds, seed=C * 1000 + M + H)
+    assert kind == "conv_tc"
+    assert_fp16_layer_close(got, ref, f"tc C{C} M{M} {H}x{W} act{act} adds{nadds}")
+
+
+SIMT_CASES = [
+    (1, 64, 40, 77, 0, 0),    # head conv
+    (1, 8, 17, 25, 1, 0),
+    (3, 64, 16, 33, 2, 0),    # chroma head
+    (4, 4, 33, 17, 0, 1),
+    (64, 4, 21, 70, 0, 0),    # tail without DepthToSpace
+    (64, 2, 9, 9, 0, 0),
+    (160, 16, 6, 40, 1, 0),   # wider than the tensor-core tiling: CUDA-core path
+]
+
+
+@pytest.mark.parametrize("C,M,H,W,act,nadds", SIMT_CASES)
+def test_cuda_core_conv_matches_fp32_reference(C, M, H, W, act, nadds):
+    kind, got, ref = _case(C, M, H, W, act, nadds, seed=C * 1000 + M + H + 7)
+    assert kind == "conv_simt"
+    assert_fp16_layer_close(got, ref, f"simt C{C} M{M} {H}x{W}")
+
+
+def test_microbench_layer_full_size():
+    """conv 64->64 + bias + ReLU on a 1080x1920 NHWC frame."""
+    kind, got, ref = _case(64, 64, 1080, 1920, 1, 0, seed=1)
+    assert kind == "conv_tc"
+    assert_fp16_layer_close(got, ref, "C1 1080p", min_exact=0.99)
+
+
+def test_repeated_launches_are_bit_identical():
+    from arthip_b200.engine import Conv3x3
+    dev = torch.device("cuda:0")
+    g = torch.Generator(device="cpu").manual_seed(5)
+    x = torch.rand(1, 270, 480, 64, generator=g).half().to(dev)
+    w = (torch.randn(64, 64, 3, 3, generator=g) * 0.06).numpy().astype(np.float16)
+    conv = Conv3x3(w, None, act=1)
+    outs = []
+    for _ in range(4):
+        o = torch.empty(1, 270, 480, 64, dtype=torch.float16, device=dev)
+        conv.run(x.data_ptr(), 270, 480, o.data_ptr(), stream=torch.cuda.current_stream().cuda_stream)
+        outs.append(o)
+    torch.cuda.synchronize()
+    for o in outs[1:]:
+        assert torch.equal(o, outs[0])
