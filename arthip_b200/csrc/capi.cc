@@ -56,10 +56,10 @@ struct ah_conv {
   ah::SimtConvWeights sw;
   ah::ConvTcPlan plan;
   const void* plan_in = nullptr;
+  const void* plan_out = nullptr;
   int plan_H = 0, plan_W = 0;
   int num_sms = 148;
   uint32_t* status = nullptr;
-  int desc_base_mode = 1;
 };
 
 extern "C" {
@@ -401,7 +401,6 @@ int ah_conv3x3_create(int device, int C, int M, const uint16_t* w, const float* 
   c->C = C;
   c->M = M;
   c->act = act;
-  if (const char* env = std::getenv("ARTHIP_DESC_BASE_MODE")) c->desc_base_mode = std::atoi(env);
   int sms = 0;
   if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) == cudaSuccess && sms > 0) c->num_sms = sms;
   c->tc = ah::conv_tc_supported(C, M, nullptr);
@@ -430,18 +429,22 @@ int ah_conv3x3_run(ah_conv* c, const void* in, int H, int W, const void* add1, c
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   cudaError_t e;
   if (c->tc) {
-    if (c->plan_in != in || c->plan_H != H || c->plan_W != W) {
+    if (c->plan_in != in || c->plan_out != out || c->plan_H != H || c->plan_W != W) {
       std::string perr;
-      if (!ah::conv_tc_plan(&c->tcw, static_cast<const __half*>(in), H, W, c->num_sms, &c->plan, &perr)) {
+      ah::ConvTcOut to;
+      to.ptr = out;
+      to.mode = (c->M % 16 == 0) ? 0 : 1;  // NHWC via TMA stores, or per-element NHWC stores
+      if (!ah::conv_tc_plan(&c->tcw, static_cast<const __half*>(in), H, W, to, c->num_sms, &c->plan, &perr)) {
         CopyOut(perr, err, errlen);
         return 1;
       }
       c->plan_in = in;
+      c->plan_out = out;
       c->plan_H = H;
       c->plan_W = W;
     }
-    e = ah::conv_tc_launch(c->plan, static_cast<const __half*>(add1), static_cast<const __half*>(add2),
-                           static_cast<__half*>(out), c->act, c->status, s, c->desc_base_mode);
+    e = ah::conv_tc_launch(c->plan, static_cast<const __half*>(add1), static_cast<const __half*>(add2), c->act,
+                           c->status, s);
   } else {
     ah::SimtOut so;
     so.ptr = out;

@@ -148,7 +148,6 @@ Engine::Engine(int device_id) : device_id_(device_id) {
   poison_ = EnvOn("VSHIP_POISON");
   sync_each_ = EnvOn("VSHIP_SYNC_EACH");
   no_graph_ = EnvOn("ARTHIP_NO_GRAPH") || prof_ || poison_ || sync_each_;
-  if (const char* e = std::getenv("ARTHIP_DESC_BASE_MODE")) desc_base_mode_ = std::atoi(e);
 }
 
 Engine::~Engine() { DestroyAll(); }
@@ -713,7 +712,7 @@ bool Engine::UploadWeights(std::string& error) {
       for (int m = 0; m < M; ++m) bias[m] = HalfToFloat(WeightHalf(bs, m));
     }
     ConvWeights cw;
-    cw.tc = !op.fuse_dts && conv_tc_supported(C, M, nullptr);
+    cw.tc = conv_tc_supported(C, M, nullptr);
     cudaError_t e = cw.tc ? conv_tc_upload(w16.data(), bias.data(), C, M, &cw.tcw)
                           : simt_conv_upload(w16.data(), bias.data(), C, M, &cw.sw);
     conv_weights_.push_back(cw);
@@ -818,8 +817,7 @@ bool Engine::EnsureBuilt(const std::vector<int64_t>& s4, std::string& error) {
   bool out_direct = false;
   if (out_op >= 0 && out_needs_convert) {
     const OpSpec& o = ops_[out_op];
-    if (o.type == OpType::DepthToSpace) out_direct = true;
-    if (o.type == OpType::Conv && !conv_weights_[conv_widx_[out_op]].tc) out_direct = true;
+    if (o.type == OpType::DepthToSpace || o.type == OpType::Conv) out_direct = true;
   }
 
   for (size_t i = 0; i < ops_.size(); ++i) {
@@ -895,11 +893,32 @@ bool Engine::EnsureBuilt(const std::vector<int64_t>& s4, std::string& error) {
             << (o.adds.empty() ? "" : (o.adds.size() == 1 ? " +add" : " +add+add")) << (o.fuse_dts ? " +dts" : "");
         d.info.flops = 2.0 * 9.0 * d.C * d.M * P;
         d.info.bytes = 2.0 * P * d.C + 2.0 * P * d.M * (1.0 + o.adds.size()) + 2.0 * (9.0 * d.C * d.M + d.M);
+        // Output form shared by both conv kernels: fused DepthToSpace / clip, and the
+        // graph-boundary layout (NCHW, model dtype) when this op produces the output.
+        d.sout.dts_b = o.fuse_dts ? o.blocksize : 1;
+        d.sout.clip = o.fuse_clip ? 1 : 0;
+        d.sout.clip_lo = o.clip_min;
+        d.sout.clip_hi = o.clip_max;
+        if (direct_here) {
+          d.sout.nchw = 1;
+          d.sout.fp32 = output_is_fp32_ ? 1 : 0;
+        }
         if (cw.tc) {
           d.kind = 0;
           d.info.kind = "conv_tc";
+          ConvTcOut to;
+          to.ptr = direct_here ? out_boundary_ : bufs_[d.out_buf];
+          const bool plain = !o.fuse_dts && !o.fuse_clip && !direct_here && d.M % 16 == 0;
+          to.mode = plain ? 0 : 1;
+          to.dts_b = d.sout.dts_b;
+          to.nchw = d.sout.nchw;
+          to.fp32 = d.sout.fp32;
+          to.clip = d.sout.clip;
+          to.clip_lo = d.sout.clip_lo;
+          to.clip_hi = d.sout.clip_hi;
           std::string perr;
-          if (!conv_tc_plan(&cw.tcw, static_cast<const __half*>(bufs_[d.in_buf]), d.H, d.W, num_sms_, &d.tc, &perr)) {
+          if (!conv_tc_plan(&cw.tcw, static_cast<const __half*>(bufs_[d.in_buf]), d.H, d.W, to, num_sms_, &d.tc,
+                            &perr)) {
             error = "conv plan failed: " + perr;
             DestroyShapeState();
             return false;
@@ -907,16 +926,6 @@ bool Engine::EnsureBuilt(const std::vector<int64_t>& s4, std::string& error) {
         } else {
           d.kind = 1;
           d.info.kind = "conv_simt";
-          const auto& os = shapes.at(o.out);
-          d.sout.dts_b = o.fuse_dts ? o.blocksize : 1;
-          d.sout.clip = o.fuse_clip ? 1 : 0;
-          d.sout.clip_lo = o.clip_min;
-          d.sout.clip_hi = o.clip_max;
-          if (direct_here) {
-            d.sout.nchw = 1;
-            d.sout.fp32 = output_is_fp32_ ? 1 : 0;
-          }
-          (void)os;
         }
         break;
       }
@@ -1005,8 +1014,7 @@ bool Engine::LaunchFrame(bool with_events, std::string& error) {
     switch (d.kind) {
       case 0:
         e = conv_tc_launch(d.tc, static_cast<const __half*>(BufPtr(d.add_buf[0])),
-                           static_cast<const __half*>(BufPtr(d.add_buf[1])), static_cast<__half*>(out), d.act,
-                           status_, s, desc_base_mode_);
+                           static_cast<const __half*>(BufPtr(d.add_buf[1])), d.act, status_, s);
         break;
       case 1: {
         SimtOut so = d.sout;

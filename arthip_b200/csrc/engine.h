@@ -163,7 +163,6 @@ class Engine {
   void* out_staging_ = nullptr;   // pinned host
   uint32_t* status_ = nullptr;    // device error word written by kernels
   cudaGraphExec_t graph_exec_ = nullptr;
-  int desc_base_mode_ = 1;
 
   // timing
   std::vector<cudaEvent_t> tevents_;

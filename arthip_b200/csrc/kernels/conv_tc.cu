@@ -1,30 +1,33 @@
 // tcgen05 implicit-GEMM 3x3 convolution (stride 1, SAME padding) for sm_100a.
 //
 // Replaces the reference's gfx1100 Winograd WMMA kernel (src/common/hip_kernels.h:143-396)
-// for every conv whose channel counts fit the tensor-core tiling (C and M multiples of 16).
+// for every conv whose input channel count fits the tensor-core tiling (C % 16 == 0,
+// C <= 128), and the narrow tail conv with its fused DepthToSpace / Clip / boundary
+// cast (the reference's dts_kernel_2d / dts_kernel_in_f32, hip_kernels.h:553-616).
 //
 // GEMM view: one output row segment of 128 pixels is the MMA M dimension, the output
-// channels are N, and K = 9 taps x C input channels. Per output row the kernel issues
-// 9 * C/16 tcgen05.mma (128 x MT x 16, fp16 in, fp32 accumulate in tensor memory).
+// channels (padded to 16) are N, and K = 9 taps x C input channels. Per output row the
+// kernel issues one bias MMA (a constant ones column times the bias row initialises the
+// accumulator) and 9 * C/16 conv MMAs (128 x MT x 16, fp16 in, fp32 accumulate in TMEM).
 //
 // Data movement:
 //  * input: one TMA tiled load per (input row, channel chunk) brings 130 pixels
 //    (the 128-pixel tile plus a 1-pixel halo each side; out-of-range pixels and rows are
-//    zero-filled by the TMA unit, which is exactly the conv's zero padding) into a ring of
-//    row slots. Each staged row feeds three consecutive output rows (ky = 0,1,2); the
-//    three horizontal taps (kx) read the same slot with the descriptor start moved by one
-//    pixel row, so nothing is re-staged.
-//  * weights: resident in shared memory for the whole (persistent) kernel, in the
-//    swizzled K-major layout the MMA reads; packed once on the host.
+//    zero-filled by the TMA unit, which is the conv's zero padding) into a ring of row
+//    slots. Each staged row feeds three output rows (ky = 0,1,2); the three horizontal
+//    taps (kx) read the same slot with the descriptor start moved by one pixel row.
+//  * weights: resident in shared memory for the whole persistent kernel, packed on the
+//    host in the swizzled K-major layout the MMA reads.
 //  * accumulators: a ring of NACC tensor-memory accumulators; the epilogue warps drain
 //    one while the MMA warp fills the next.
-//  * epilogue: tcgen05.ld -> +bias -> fp16 rounding (the conv node's output) -> ReLU or
-//    SiLU -> up to two residual adds (each rounded to fp16, as the ONNX Add nodes are)
-//    -> 16-byte NHWC stores.
+//  * epilogue (8 warps; two per TMEM lane quarter, each taking alternate 32-channel
+//    groups): tcgen05.ld -> fp16 rounding (the conv node output) -> ReLU / SiLU -> up to
+//    two residual adds (fp16 adds, as the ONNX Add nodes) -> swizzled staging tile ->
+//    TMA store (mode 0), or DepthToSpace / clip / fp32 per-element stores (mode 1).
 //
-// Warp roles (192 threads): warp 0 = TMA producer, warp 1 = TMEM allocator + MMA issuer
-// (one thread), warps 2..5 = epilogue (each owns the TMEM lane quarter warp%4).
-// Work: the (strip, row) space is split into contiguous ranges, one per CTA.
+// Warp roles (320 threads): warp 0 = TMA producer, warp 1 = TMEM allocator + MMA issuer
+// (one thread), warps 2..9 = epilogue. Work: the (strip, row) space is split into
+// contiguous ranges, one per CTA; every pipeline wait is time-bounded.
 
 #include <algorithm>
 #include <cstdio>
@@ -39,20 +42,24 @@ namespace {
 
 constexpr int kMaxSlots = 8;
 constexpr int kMaxAcc = 4;
-constexpr int kThreads = 192;
+constexpr int kEpiWarps = 8;
+constexpr int kThreads = 64 + 32 * kEpiWarps;
 constexpr int kSmemLimit = 232448;  // 227 KB opt-in dynamic shared memory per block
+constexpr int kStageTile = 2048;    // one 32-pixel x 32-channel fp16 staging tile
 
 struct ConvTcArgs {
   CUtensorMap maps[kTcMaxChunks];
+  CUtensorMap out_map32;
+  CUtensorMap out_map16;
   const uint8_t* wpack;
   const float* bias;
   const __half* add1;
   const __half* add2;
-  __half* out;
   uint32_t* status;
+  ConvTcOut out;
   long long gofs[9 * kTcMaxChunks];
   int wofs[9 * kTcMaxChunks];
-  int H, W, M, MT;
+  int H, W, M, Mpad, MT;
   int nchunks;
   int rowbytes[kTcMaxChunks];
   int layout[kTcMaxChunks];
@@ -63,10 +70,9 @@ struct ConvTcArgs {
   int slot_tx;  // bytes one row load delivers (all chunks, full boxes)
   int nslots;
   int w_smem_bytes;
-  int n_strips;
+  int ones_off, biasb_off, stage_off, stage_per_warp;
   long long rows_total;
   int act;
-  int desc_base_mode;
   int nacc, acc_stride;
   uint32_t tmem_cols;
 };
@@ -90,25 +96,47 @@ struct SegIter {
   }
 };
 
-__device__ __forceinline__ float h2f(__half h) { return __half2float(h); }
 __device__ __forceinline__ float r16(float v) { return __half2float(__float2half_rn(v)); }
 
-__device__ __forceinline__ void unpack8(const uint4& u, float (&f)[8]) {
-  const __half2* h = reinterpret_cast<const __half2*>(&u);
+// Byte offset of 16-byte granule j of row r in a swizzled K-major tile with `rb`-byte rows
+// (128B / 64B / 32B swizzle: the granule index is XORed with address bits 7.. of the row,
+// for a tile that starts on a 1024-byte boundary).
+__host__ __device__ __forceinline__ uint32_t swz_granule(uint32_t r, uint32_t j, uint32_t rb) {
+  const uint32_t phase = rb == 128 ? (r & 7u) : (rb == 64 ? ((r >> 1) & 3u) : ((r >> 2) & 1u));
+  return r * rb + ((j ^ phase) << 4);
+}
+
+__device__ __forceinline__ void hadd8(uint32_t (&h)[4], const __half* src) {
+  const uint4 u = __ldg(reinterpret_cast<const uint4*>(src));
+  const uint32_t* q = reinterpret_cast<const uint32_t*>(&u);
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
-    float2 t = __half22float2(h[i]);
-    f[2 * i] = t.x;
-    f[2 * i + 1] = t.y;
+    __half2 v = __hadd2(*reinterpret_cast<__half2*>(&h[i]), *reinterpret_cast<const __half2*>(&q[i]));
+    h[i] = *reinterpret_cast<uint32_t*>(&v);
   }
 }
 
-__device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
-  uint4 u;
-  __half2* h = reinterpret_cast<__half2*>(&u);
+// Activation + residual adds on 8 channels held as 4 half2 (the fp16-rounded conv output).
+__device__ __forceinline__ void epilogue8(uint32_t (&h)[4], int act, const __half* a1, const __half* a2) {
+  if (act == kActSilu) {
 #pragma unroll
-  for (int i = 0; i < 4; ++i) h[i] = __floats2half2_rn(f[2 * i], f[2 * i + 1]);
-  return u;
+    for (int i = 0; i < 4; ++i) {
+      const float2 t = __half22float2(*reinterpret_cast<__half2*>(&h[i]));
+      const float s0 = r16(1.f / (1.f + __expf(-t.x)));
+      const float s1 = r16(1.f / (1.f + __expf(-t.y)));
+      __half2 o = __floats2half2_rn(t.x * s0, t.y * s1);
+      h[i] = *reinterpret_cast<uint32_t*>(&o);
+    }
+  } else if (act == kActRelu) {
+    const __half2 z = __float2half2_rn(0.f);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      __half2 v = __hmax2(*reinterpret_cast<__half2*>(&h[i]), z);
+      h[i] = *reinterpret_cast<uint32_t*>(&v);
+    }
+  }
+  if (a1) hadd8(h, a1);
+  if (a2) hadd8(h, a2);
 }
 
 __global__ void __launch_bounds__(kThreads, 1) conv3x3_tc_kernel(const __grid_constant__ ConvTcArgs a) {
@@ -116,8 +144,10 @@ __global__ void __launch_bounds__(kThreads, 1) conv3x3_tc_kernel(const __grid_co
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sW = smem;
   uint8_t* sA = smem + a.w_smem_bytes;
-  float* sBias = reinterpret_cast<float*>(sA + a.nslots * a.slot_bytes);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sBias + 256);
+  uint8_t* sOnes = smem + a.ones_off;
+  uint8_t* sBiasB = smem + a.biasb_off;
+  uint8_t* sStage = smem + a.stage_off;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sStage + kEpiWarps * a.stage_per_warp);
   uint64_t* full = bars;
   uint64_t* empty = bars + kMaxSlots;
   uint64_t* accf = bars + 2 * kMaxSlots;
@@ -140,7 +170,7 @@ __global__ void __launch_bounds__(kThreads, 1) conv3x3_tc_kernel(const __grid_co
     }
     for (int i = 0; i < NACC; ++i) {
       ptx::mbar_init(ptx::smem_u32(&accf[i]), 1);
-      ptx::mbar_init(ptx::smem_u32(&acce[i]), 4);
+      ptx::mbar_init(ptx::smem_u32(&acce[i]), kEpiWarps);
     }
     ptx::mbar_init(ptx::smem_u32(wbar), 1);
     ptx::mbar_init(ptx::smem_u32(donebar), 1);
@@ -154,7 +184,21 @@ __global__ void __launch_bounds__(kThreads, 1) conv3x3_tc_kernel(const __grid_co
     ptx::tmem_alloc(ptx::smem_u32(tmem_slot), a.tmem_cols);
     ptx::tmem_relinquish();
   }
-  for (int i = threadIdx.x; i < a.MT; i += blockDim.x) sBias[i] = a.bias[m0 + i];
+  // Bias operands (32-byte swizzled rows, 16 K elements): a ones column for the 128
+  // pixel rows, and the bias as column 0 of the MT output-channel rows.
+  for (int r = threadIdx.x; r < kTcTilePx; r += blockDim.x) {
+    uint4* row = reinterpret_cast<uint4*>(sOnes + r * 32);
+    row[0] = make_uint4(0, 0, 0, 0);
+    row[1] = make_uint4(0, 0, 0, 0);
+    *reinterpret_cast<__half*>(sOnes + swz_granule(r, 0, 32)) = __float2half(1.f);
+  }
+  for (int r = threadIdx.x; r < a.MT; r += blockDim.x) {
+    uint4* row = reinterpret_cast<uint4*>(sBiasB + r * 32);
+    row[0] = make_uint4(0, 0, 0, 0);
+    row[1] = make_uint4(0, 0, 0, 0);
+    *reinterpret_cast<__half*>(sBiasB + swz_granule(r, 0, 32)) = __float2half(a.bias[m0 + r]);
+  }
+  ptx::fence_proxy_async_smem();  // the tensor core reads the generic writes above
   ptx::tc_fence_before();
   __syncthreads();
   ptx::tc_fence_after();
@@ -208,6 +252,8 @@ __global__ void __launch_bounds__(kThreads, 1) conv3x3_tc_kernel(const __grid_co
       const uint32_t idesc = ptx::idesc_f16_f32(kTcTilePx, a.MT);
       const uint32_t sA_u = ptx::smem_u32(sA);
       const uint32_t sW_u = ptx::smem_u32(sW);
+      const uint64_t ones_desc = ptx::smem_desc(ptx::smem_u32(sOnes), 6, 256);
+      const uint64_t biasb_desc = ptx::smem_desc(ptx::smem_u32(sBiasB), 6, 256);
       bool ok = ptx::mbar_wait(ptx::smem_u32(wbar), 0, abort_flag);
       uint32_t g_base = 0, acc_cnt = 0;
       SegIter it{t0, t1, a.H};
@@ -224,7 +270,7 @@ __global__ void __launch_bounds__(kThreads, 1) conv3x3_tc_kernel(const __grid_co
           if (!ok) break;
           ptx::tc_fence_after();
           const uint32_t d = tmem_base + acc * a.acc_stride;
-          uint32_t accumulate = 0;
+          ptx::mma_f16_ss(d, ones_desc, biasb_desc, idesc, 0);  // D = bias
           for (int ky = 0; ky < 3; ++ky) {
             const uint32_t a_slot = sA_u + ((g_base + i + ky) % S) * a.slot_bytes;
             for (int k = 0; k < a.nchunks; ++k) {
@@ -235,10 +281,9 @@ __global__ void __launch_bounds__(kThreads, 1) conv3x3_tc_kernel(const __grid_co
               for (int kx = 0; kx < 3; ++kx) {
                 const uint32_t b_blk = sW_u + a.wofs[(ky * 3 + kx) * a.nchunks + k];
                 for (int kb = 0; kb < a.kblocks[k]; ++kb) {
-                  const uint64_t ad = ptx::smem_desc(a_chunk + kx * rb + kb * 32u, lay, sbo, a.desc_base_mode);
-                  const uint64_t bd = ptx::smem_desc(b_blk + kb * 32u, lay, sbo, a.desc_base_mode);
-                  ptx::mma_f16_ss(d, ad, bd, idesc, accumulate);
-                  accumulate = 1;
+                  const uint64_t ad = ptx::smem_desc(a_chunk + kx * rb + kb * 32u, lay, sbo);
+                  const uint64_t bd = ptx::smem_desc(b_blk + kb * 32u, lay, sbo);
+                  ptx::mma_f16_ss(d, ad, bd, idesc, 1);
                 }
               }
             }
@@ -259,15 +304,21 @@ __global__ void __launch_bounds__(kThreads, 1) conv3x3_tc_kernel(const __grid_co
     }
     __syncwarp();
   } else {
-    // ---------------- epilogue (warps 2..5) ----------------
-    const int q = warp & 3;  // tensor-memory lane quarter this warp may access
-    const int p = q * 32 + lane;
+    // ---------------- epilogue (warps 2..9) ----------------
+    const int e = warp - 2;
+    const int q = warp & 3;   // tensor-memory lane quarter this warp may access
+    const int half = e >> 2;  // this warp takes channel groups half, half+2, ...
+    const int ngroups = (a.MT + 31) / 32;
+    uint8_t* stage = sStage + e * a.stage_per_warp;
+    const ConvTcOut& o = a.out;
     uint32_t acc_cnt = 0;
     SegIter it{t0, t1, a.H};
     Segment sg;
     bool ok = true;
+    bool stores_pending = false;
     while (ok && it.next(sg)) {
-      const int x = sg.strip * kTcTilePx + p;
+      const int xw = sg.strip * kTcTilePx + q * 32;  // first pixel of this warp's 32
+      const int x = xw + lane;
       const bool valid = x < a.W;
       for (int y = sg.ya; y < sg.yb; ++y) {
         const uint32_t acc = acc_cnt % NACC;
@@ -279,51 +330,84 @@ __global__ void __launch_bounds__(kThreads, 1) conv3x3_tc_kernel(const __grid_co
           break;
         }
         ptx::tc_fence_after();
+        if (o.mode == 0 && stores_pending) {
+          if (lane == 0) ptx::bulk_wait_group_read0();  // the staging tiles are free again
+          __syncwarp();
+        }
         const size_t pix = static_cast<size_t>(y) * a.W + (valid ? x : 0);
-        const size_t obase = pix * a.M + m0;
-        for (int cc = 0; cc < a.MT; cc += 32) {
-          uint32_t r[32];
-          const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * a.acc_stride + cc;
-          const int ncols = min(32, a.MT - cc);
-          if (ncols == 32) ptx::tmem_ld_32x32b_x32(taddr, r);
-          else ptx::tmem_ld_32x32b_x16(taddr, r);
+        for (int g = half, k = 0; g < ngroups; g += 2, ++k) {
+          const int cw = min(32, a.MT - g * 32);
+          uint32_t rr[32];
+          const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * a.acc_stride + g * 32;
+          if (cw == 32) ptx::tmem_ld_32x32b_x32(taddr, rr);
+          else ptx::tmem_ld_32x32b_x16(taddr, rr);
           ptx::tmem_wait_ld();
-          if (valid) {
-            for (int g8 = 0; g8 < ncols; g8 += 8) {
-              float v[8];
+          if (g + 2 >= ngroups) {  // this warp's last group: release the accumulator
+            ptx::tc_fence_before();
+            __syncwarp();
+            if (lane == 0) ptx::mbar_arrive(ptx::smem_u32(&acce[acc]));
+          }
+          const int cbase = m0 + g * 32;
+          if (o.mode == 0) {
+            uint8_t* st = stage + k * kStageTile;
+            const uint32_t rb = cw * 2;
 #pragma unroll
-              for (int j = 0; j < 8; ++j) {
-                float t = r16(__uint_as_float(r[g8 + j]) + sBias[cc + g8 + j]);
-                if (a.act == kActRelu) {
-                  t = fmaxf(t, 0.f);
-                } else if (a.act == kActSilu) {
-                  const float sg2 = r16(1.f / (1.f + __expf(-t)));
-                  t = r16(t * sg2);
-                }
-                v[j] = t;
-              }
-              if (a.add1) {
-                float ad[8];
-                unpack8(*reinterpret_cast<const uint4*>(a.add1 + obase + cc + g8), ad);
+            for (int j8 = 0; j8 < 32; j8 += 8) {
+              if (j8 >= cw) break;
+              uint32_t h[4];
 #pragma unroll
-                for (int j = 0; j < 8; ++j) v[j] = r16(v[j] + ad[j]);
+              for (int i = 0; i < 4; ++i) {
+                __half2 v = __floats2half2_rn(__uint_as_float(rr[j8 + 2 * i]), __uint_as_float(rr[j8 + 2 * i + 1]));
+                h[i] = *reinterpret_cast<uint32_t*>(&v);
               }
-              if (a.add2) {
-                float ad[8];
-                unpack8(*reinterpret_cast<const uint4*>(a.add2 + obase + cc + g8), ad);
+              const __half* a1 = (a.add1 && valid) ? a.add1 + pix * a.M + cbase + j8 : nullptr;
+              const __half* a2 = (a.add2 && valid) ? a.add2 + pix * a.M + cbase + j8 : nullptr;
+              epilogue8(h, a.act, a1, a2);
+              *reinterpret_cast<uint4*>(st + swz_granule(lane, j8 >> 3, rb)) = make_uint4(h[0], h[1], h[2], h[3]);
+            }
+          } else if (valid) {
+            // Narrow tails: per-element DepthToSpace (DCR) / clip / dtype / layout.
+            const int b = o.dts_b;
+            const int cout = a.M / (b * b);
+            const long long Ho = static_cast<long long>(a.H) * b, Wo = static_cast<long long>(a.W) * b;
 #pragma unroll
-                for (int j = 0; j < 8; ++j) v[j] = r16(v[j] + ad[j]);
-              }
-              *reinterpret_cast<uint4*>(a.out + obase + cc + g8) = pack8(v);
+            for (int j = 0; j < 32; ++j) {
+              const int m = cbase + j;
+              if (j >= cw || m >= a.M) break;
+              float t = r16(__uint_as_float(rr[j]));
+              if (a.act == kActRelu) t = fmaxf(t, 0.f);
+              else if (a.act == kActSilu) t = r16(t * r16(1.f / (1.f + __expf(-t))));
+              if (a.add1) t = r16(t + __half2float(a.add1[pix * a.M + m]));
+              if (a.add2) t = r16(t + __half2float(a.add2[pix * a.M + m]));
+              if (o.clip) t = fminf(fmaxf(t, o.clip_lo), o.clip_hi);
+              const int rq = m / cout, c = m - rq * cout;
+              const int r_ = rq / b, q_ = rq - r_ * b;
+              const long long oy = static_cast<long long>(y) * b + r_, ox = static_cast<long long>(x) * b + q_;
+              const long long idx =
+                  o.nchw ? ((static_cast<long long>(c) * Ho + oy) * Wo + ox) : ((oy * Wo + ox) * cout + c);
+              if (o.fp32) static_cast<float*>(o.ptr)[idx] = t;
+              else static_cast<__half*>(o.ptr)[idx] = __float2half_rn(t);
             }
           }
         }
-        ptx::tc_fence_before();
-        __syncwarp();
-        if (lane == 0) ptx::mbar_arrive(ptx::smem_u32(&acce[acc]));
+        if (o.mode == 0) {
+          ptx::fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0 && xw < a.W) {
+            for (int g = half, k = 0; g < ngroups; g += 2, ++k) {
+              const int cw = min(32, a.MT - g * 32);
+              const uint32_t src = ptx::smem_u32(stage + k * kStageTile);
+              ptx::tma_store_3d(cw == 32 ? &a.out_map32 : &a.out_map16, src, m0 + g * 32, xw, y);
+            }
+            ptx::bulk_commit_group();
+          }
+          stores_pending = true;
+        }
         ++acc_cnt;
       }
     }
+    if (o.mode == 0 && lane == 0) ptx::bulk_wait_group0();
+    __syncwarp();
   }
 
   ptx::tc_fence_before();
@@ -381,19 +465,20 @@ void make_chunks(int C, ConvTcWeights* w) {
   }
 }
 
-// Byte position of element (row m, channel k) inside one swizzled K-major block.
-// Rows are `rb` bytes; 16-byte granule j of row m is stored at granule j ^ phase(m),
-// where the phase is taken from address bits 7.. of the row (the 128B/64B/32B swizzle
-// patterns repeat every 1024/512/256 bytes).
-size_t swz_offset(int m, int k, int rb) {
-  const size_t row = static_cast<size_t>(m) * rb;
-  const int j = (k * 2) / 16;
-  const int e = (k * 2) % 16;
-  int phase;
-  if (rb == 128) phase = m & 7;
-  else if (rb == 64) phase = (m >> 1) & 3;
-  else phase = (m >> 2) & 1;
-  return row + static_cast<size_t>((j ^ phase) * 16 + e);
+bool encode(EncodeTiledFn enc, CUtensorMap* map, const void* base, int C, int W, int H, int box_c, int box_px,
+            std::string* err) {
+  cuuint64_t gdim[3] = {static_cast<cuuint64_t>(C), static_cast<cuuint64_t>(W), static_cast<cuuint64_t>(H)};
+  cuuint64_t gstride[2] = {static_cast<cuuint64_t>(C) * 2, static_cast<cuuint64_t>(W) * C * 2};
+  cuuint32_t box[3] = {static_cast<cuuint32_t>(box_c), static_cast<cuuint32_t>(box_px), 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(base), gdim, gstride, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle_for(box_c), CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    if (err) *err = "cuTensorMapEncodeTiled failed (code " + std::to_string(static_cast<int>(r)) + ")";
+    return false;
+  }
+  return true;
 }
 
 }  // namespace
@@ -405,8 +490,8 @@ bool conv_tc_supported(int C, int M, std::string* why) {
     if (why) *why = "tensor-core conv needs C % 16 == 0 and C <= 128";
     return false;
   }
-  if (M % 16 != 0 || M > 256) {
-    if (why) *why = "tensor-core conv needs M % 16 == 0 and M <= 256";
+  if (M < 1 || M > 256) {
+    if (why) *why = "tensor-core conv needs 1 <= M <= 256";
     return false;
   }
   return true;
@@ -416,11 +501,13 @@ std::vector<uint8_t> conv_tc_pack_host(const uint16_t* w_oihw, int C, int M, Con
   make_chunks(C, L);
   L->C = C;
   L->M = M;
+  L->Mpad = round_up(M, 16);
+  const int Mp = L->Mpad;
   long long off = 0;
   for (int t = 0; t < 9; ++t)
     for (int k = 0; k < L->nchunks; ++k) {
       L->gofs[t * L->nchunks + k] = off;
-      off += static_cast<long long>(M) * L->chunk[k].rowbytes;
+      off += static_cast<long long>(Mp) * L->chunk[k].rowbytes;
     }
   std::vector<uint8_t> img(static_cast<size_t>(off), 0);
   for (int t = 0; t < 9; ++t) {
@@ -431,7 +518,7 @@ std::vector<uint8_t> conv_tc_pack_host(const uint16_t* w_oihw, int C, int M, Con
         for (int kk = 0; kk < ch.cw; ++kk) {
           const int c = ch.c0 + kk;
           const uint16_t v = w_oihw[(static_cast<size_t>(m) * C + c) * 9 + t];
-          std::memcpy(blk + swz_offset(m, kk, ch.rowbytes), &v, 2);
+          std::memcpy(blk + swz_granule(m, (kk * 2) / 16, ch.rowbytes) + (kk * 2) % 16, &v, 2);
         }
     }
   }
@@ -445,11 +532,11 @@ cudaError_t conv_tc_upload(const uint16_t* w_oihw, const float* bias, int C, int
   if (e != cudaSuccess) return e;
   e = cudaMemcpy(out->wpack, img.data(), img.size(), cudaMemcpyHostToDevice);
   if (e != cudaSuccess) return e;
-  std::vector<float> b(M, 0.f);
+  std::vector<float> b(out->Mpad, 0.f);
   if (bias) std::memcpy(b.data(), bias, sizeof(float) * M);
-  e = cudaMalloc(&out->bias, sizeof(float) * M);
+  e = cudaMalloc(&out->bias, sizeof(float) * out->Mpad);
   if (e != cudaSuccess) return e;
-  return cudaMemcpy(out->bias, b.data(), sizeof(float) * M, cudaMemcpyHostToDevice);
+  return cudaMemcpy(out->bias, b.data(), sizeof(float) * out->Mpad, cudaMemcpyHostToDevice);
 }
 
 void conv_tc_free(ConvTcWeights* w) {
@@ -459,39 +546,51 @@ void conv_tc_free(ConvTcWeights* w) {
   w->bias = nullptr;
 }
 
-bool conv_tc_plan(const ConvTcWeights* w, const __half* in, int H, int W, int num_sms, ConvTcPlan* P,
-                  std::string* err) {
+bool conv_tc_plan(const ConvTcWeights* w, const __half* in, int H, int W, const ConvTcOut& out, int num_sms,
+                  ConvTcPlan* P, std::string* err) {
   EncodeTiledFn enc = get_encode_fn();
   if (!enc) {
     if (err) *err = "cuTensorMapEncodeTiled is unavailable from the CUDA driver";
     return false;
   }
-  if ((reinterpret_cast<uintptr_t>(in) & 15u) != 0) {
-    if (err) *err = "tensor-core conv input must be 16-byte aligned";
+  if ((reinterpret_cast<uintptr_t>(in) & 15u) != 0 ||
+      (out.mode == 0 && (reinterpret_cast<uintptr_t>(out.ptr) & 15u) != 0)) {
+    if (err) *err = "tensor-core conv buffers must be 16-byte aligned";
+    return false;
+  }
+  if (out.mode == 0 && w->M != w->Mpad) {
+    if (err) *err = "tensor-core conv NHWC output needs M % 16 == 0";
     return false;
   }
   P->w = w;
   P->H = H;
   P->W = W;
+  P->out = out;
   int slot_bytes = 0;
   for (int k = 0; k < w->nchunks; ++k) slot_bytes += w->chunk[k].area;
   P->slot_bytes = slot_bytes;
-  const int fixed = 1024 /*align slack*/ + 256 * 4 /*bias*/ + 256 /*barriers + flags*/;
-  // Largest channel slice (divisor of M, multiple of 16) whose weights and >= 4 row
-  // slots fit in shared memory; 3 slots is the functional minimum.
-  int chosen = 0, slots = 0, wbytes_chosen = 0;
-  for (int nsplit = 1; nsplit <= w->M / 16 && !chosen; ++nsplit) {
-    if (w->M % nsplit) continue;
-    const int MT = w->M / nsplit;
+  const int fixed = 1024 /*align slack*/ + 4096 /*ones tile*/ + 512 /*barriers + flags*/;
+  // Largest channel slice (divisor of Mpad, multiple of 16) whose weights, bias tile,
+  // staging tiles and >= 4 input-row slots fit in shared memory (3 is the minimum).
+  int chosen = 0, slots = 0;
+  for (int nsplit = 1; nsplit <= w->Mpad / 16 && !chosen; ++nsplit) {
+    if (w->Mpad % nsplit) continue;
+    const int MT = w->Mpad / nsplit;
     if (MT % 16) continue;
     int wb = 0;
     for (int t = 0; t < 9; ++t)
       for (int k = 0; k < w->nchunks; ++k) wb += round_up(MT * w->chunk[k].rowbytes, 1024);
-    for (int s = 4; s >= 3; --s) {
-      if (wb + s * slot_bytes + fixed <= kSmemLimit) {
+    const int ngroups = (MT + 31) / 32;
+    const int stage = out.mode == 0 ? kEpiWarps * ((ngroups + 1) / 2) * kStageTile : 0;
+    const int base = wb + stage + round_up(MT * 32, 1024) + fixed;
+    bool can_split = false;
+    for (int ns = nsplit + 1; ns <= w->Mpad / 16; ++ns)
+      if (w->Mpad % ns == 0 && (w->Mpad / ns) % 16 == 0) can_split = true;
+    for (int s = kMaxSlots; s >= 3; --s) {
+      if (base + s * slot_bytes <= kSmemLimit) {
+        if (s < 4 && can_split) break;  // rather split the channels than run a 3-slot ring
         chosen = MT;
         slots = s;
-        wbytes_chosen = wb;
         break;
       }
     }
@@ -501,16 +600,25 @@ bool conv_tc_plan(const ConvTcWeights* w, const __half* in, int H, int W, int nu
     return false;
   }
   P->MT = chosen;
-  P->n_msplit = w->M / chosen;
+  P->n_msplit = w->Mpad / chosen;
   P->nslots = slots;
-  P->w_smem_bytes = wbytes_chosen;
   int off = 0;
   for (int t = 0; t < 9; ++t)
     for (int k = 0; k < w->nchunks; ++k) {
       P->wofs[t * w->nchunks + k] = off;
       off += round_up(chosen * w->chunk[k].rowbytes, 1024);
     }
-  P->smem_bytes = static_cast<size_t>(wbytes_chosen + slots * slot_bytes + fixed);
+  P->w_smem_bytes = off;
+  off += slots * slot_bytes;
+  P->ones_off = off;
+  off += 4096;
+  P->biasb_off = off;
+  off += round_up(chosen * 32, 1024);
+  P->stage_off = off;
+  const int ngroups = (chosen + 31) / 32;
+  P->stage_per_warp = out.mode == 0 ? ((ngroups + 1) / 2) * kStageTile : 0;
+  off += kEpiWarps * P->stage_per_warp;
+  P->smem_bytes = static_cast<size_t>(off) + 512 + 1024;
   P->acc_stride = round_up(chosen, 32);
   P->nacc = (4 * P->acc_stride <= 512) ? 4 : 2;
   int cols = 32;
@@ -522,36 +630,38 @@ bool conv_tc_plan(const ConvTcWeights* w, const __half* in, int H, int W, int nu
   if (gx > rows_total) gx = rows_total;
   P->grid_x = static_cast<int>(gx);
 
-  const int C = w->C;
-  for (int k = 0; k < w->nchunks; ++k) {
-    const ConvTcChunk& ch = w->chunk[k];
-    cuuint64_t gdim[3] = {static_cast<cuuint64_t>(C), static_cast<cuuint64_t>(W), static_cast<cuuint64_t>(H)};
-    cuuint64_t gstride[2] = {static_cast<cuuint64_t>(C) * 2, static_cast<cuuint64_t>(W) * C * 2};
-    cuuint32_t box[3] = {static_cast<cuuint32_t>(ch.cw), static_cast<cuuint32_t>(kTcBoxPx), 1};
-    cuuint32_t estr[3] = {1, 1, 1};
-    CUresult r = enc(&P->maps[k], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<__half*>(in), gdim, gstride, box,
-                     estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle_for(ch.cw), CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (r != CUDA_SUCCESS) {
-      if (err) *err = "cuTensorMapEncodeTiled failed (code " + std::to_string(static_cast<int>(r)) + ")";
+  for (int k = 0; k < w->nchunks; ++k)
+    if (!encode(enc, &P->maps[k], in, w->C, W, H, w->chunk[k].cw, kTcBoxPx, err)) return false;
+  if (out.mode == 0) {
+    if (chosen >= 32 && !encode(enc, &P->out_map32, out.ptr, w->M, W, H, 32, 32, err)) return false;
+    if (chosen % 32 == 16 && !encode(enc, &P->out_map16, out.ptr, w->M, W, H, 16, 32, err)) return false;
+  }
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaError_t e = cudaFuncSetAttribute(conv3x3_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
+    if (e != cudaSuccess) {
+      if (err) *err = std::string("cudaFuncSetAttribute failed: ") + cudaGetErrorString(e);
       return false;
     }
+    attr_set = true;
   }
   return true;
 }
 
-cudaError_t conv_tc_launch(const ConvTcPlan& P, const __half* add1, const __half* add2, __half* out, int act,
-                           uint32_t* status, cudaStream_t stream, int desc_base_mode) {
+cudaError_t conv_tc_launch(const ConvTcPlan& P, const __half* add1, const __half* add2, int act, uint32_t* status,
+                           cudaStream_t stream) {
   const ConvTcWeights* w = P.w;
   ConvTcArgs a;
   std::memset(&a, 0, sizeof(a));
   for (int k = 0; k < w->nchunks; ++k) a.maps[k] = P.maps[k];
+  a.out_map32 = P.out_map32;
+  a.out_map16 = P.out_map16;
   a.wpack = static_cast<const uint8_t*>(w->wpack);
   a.bias = w->bias;
   a.add1 = add1;
   a.add2 = add2;
-  a.out = out;
   a.status = status;
+  a.out = P.out;
   for (int i = 0; i < 9 * w->nchunks; ++i) {
     a.gofs[i] = w->gofs[i];
     a.wofs[i] = P.wofs[i];
@@ -559,6 +669,7 @@ cudaError_t conv_tc_launch(const ConvTcPlan& P, const __half* add1, const __half
   a.H = P.H;
   a.W = P.W;
   a.M = w->M;
+  a.Mpad = w->Mpad;
   a.MT = P.MT;
   a.nchunks = w->nchunks;
   int tx = 0;
@@ -574,20 +685,15 @@ cudaError_t conv_tc_launch(const ConvTcPlan& P, const __half* add1, const __half
   a.slot_tx = tx;
   a.nslots = P.nslots;
   a.w_smem_bytes = P.w_smem_bytes;
-  a.n_strips = (P.W + kTcTilePx - 1) / kTcTilePx;
-  a.rows_total = static_cast<long long>(a.n_strips) * P.H;
+  a.ones_off = P.ones_off;
+  a.biasb_off = P.biasb_off;
+  a.stage_off = P.stage_off;
+  a.stage_per_warp = P.stage_per_warp;
+  a.rows_total = static_cast<long long>((P.W + kTcTilePx - 1) / kTcTilePx) * P.H;
   a.act = act;
-  a.desc_base_mode = desc_base_mode;
   a.nacc = P.nacc;
   a.acc_stride = P.acc_stride;
   a.tmem_cols = static_cast<uint32_t>(P.tmem_cols);
-
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(conv3x3_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
-    if (e != cudaSuccess) return e;
-    attr_set = true;
-  }
   dim3 grid(P.grid_x, P.n_msplit);
   conv3x3_tc_kernel<<<grid, kThreads, P.smem_bytes, stream>>>(a);
   return cudaGetLastError();

@@ -36,15 +36,30 @@ struct ConvTcChunk {
 // Everything the kernel needs that depends only on (C, M, weights): built once per model.
 struct ConvTcWeights {
   int C = 0, M = 0;
+  int Mpad = 0;                // M rounded up to 16 (zero weights and bias in the padding)
   int nchunks = 0;
   ConvTcChunk chunk[kTcMaxChunks];
-  void* wpack = nullptr;       // device: [tap][chunk] blocks of M swizzled rows
+  void* wpack = nullptr;       // device: [tap][chunk] blocks of Mpad swizzled rows
   size_t wpack_bytes = 0;
   long long gofs[9 * kTcMaxChunks] = {};  // byte offset of each (tap, chunk) block
-  float* bias = nullptr;       // device: M fp32 (fp16-rounded values)
+  float* bias = nullptr;       // device: Mpad fp32 (fp16-rounded values)
 };
 
-// Per (layer, input buffer, frame size) launch plan.
+// Output of a tensor-core conv launch.
+struct ConvTcOut {
+  void* ptr = nullptr;
+  // 0: NHWC fp16 [H][W][M], written with TMA stores from a swizzled staging tile.
+  // 1: per-element stores: DepthToSpace (DCR, block dts_b; 1 = none), optional clip,
+  //    fp16 or fp32, NCHW (graph boundary) or NHWC. Used by narrow tails.
+  int mode = 0;
+  int dts_b = 1;
+  int nchw = 0;
+  int fp32 = 0;
+  int clip = 0;
+  float clip_lo = 0.f, clip_hi = 0.f;
+};
+
+// Per (layer, buffers, frame size) launch plan.
 struct ConvTcPlan {
   const ConvTcWeights* w = nullptr;
   int H = 0, W = 0;
@@ -53,10 +68,13 @@ struct ConvTcPlan {
   int slot_bytes = 0;
   int wofs[9 * kTcMaxChunks] = {};  // smem offset of each (tap, chunk) weight block
   int w_smem_bytes = 0;
+  int ones_off = 0, biasb_off = 0, stage_off = 0, stage_per_warp = 0;
   size_t smem_bytes = 0;
   int nacc = 0, acc_stride = 0, tmem_cols = 0;
   int grid_x = 0;
+  ConvTcOut out;
   CUtensorMap maps[kTcMaxChunks];
+  CUtensorMap out_map32, out_map16;
 };
 
 // Returns true when the tensor-core kernel covers (C, M); otherwise fills `why`.
@@ -67,11 +85,12 @@ cudaError_t conv_tc_upload(const uint16_t* w_oihw_f16, const float* bias_or_null
 void conv_tc_free(ConvTcWeights* w);
 // Host-only packing (exposed for tests): returns the packed byte image.
 std::vector<uint8_t> conv_tc_pack_host(const uint16_t* w_oihw_f16, int C, int M, ConvTcWeights* layout);
-// Builds the per-frame plan (tensor maps over `in`). Fails with a message when smem cannot fit.
-bool conv_tc_plan(const ConvTcWeights* w, const __half* in, int H, int W, int num_sms, ConvTcPlan* plan,
-                  std::string* err);
-cudaError_t conv_tc_launch(const ConvTcPlan& plan, const __half* add1, const __half* add2, __half* out,
-                           int act, uint32_t* status, cudaStream_t stream, int desc_base_mode = 1);
+// Builds the per-frame plan (tensor maps over `in` and, for mode 0, `out.ptr`).
+// Fails with a message when the tiles cannot fit in shared memory.
+bool conv_tc_plan(const ConvTcWeights* w, const __half* in, int H, int W, const ConvTcOut& out, int num_sms,
+                  ConvTcPlan* plan, std::string* err);
+cudaError_t conv_tc_launch(const ConvTcPlan& plan, const __half* add1, const __half* add2, int act,
+                           uint32_t* status, cudaStream_t stream);
 
 // ---------------------------------------------------------------------------
 // CUDA-core convolution for narrow layers (conv_simt.cu): C==1 heads, small M

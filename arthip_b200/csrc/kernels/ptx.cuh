@@ -91,6 +91,31 @@ __device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_
       : "memory");
 }
 
+// TMA tiled store (shared -> global), tracked by this thread's bulk-async groups.
+// Out-of-range parts of the box are not written.
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, uint32_t src, int c0, int c1, int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.global.shared::cta.tile.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(src), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+
+__device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+
+// Wait until no bulk store of this thread still reads shared memory.
+__device__ __forceinline__ void bulk_wait_group_read0() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+
+// Wait until every bulk store of this thread has completed.
+__device__ __forceinline__ void bulk_wait_group0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+// Make this thread's generic-proxy shared-memory writes visible to the async (TMA) proxy.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
 __device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
@@ -176,17 +201,20 @@ __device__ __forceinline__ void tmem_ld_32x32b_x16(uint32_t taddr, uint32_t (&r)
 //   bits 16-29  leading-dimension byte offset >> 4 (unused for swizzled K-major; 1)
 //   bits 32-45  stride-dimension byte offset >> 4 (distance between 8-row groups)
 //   bits 46-47  descriptor version (1 on sm_100)
-//   bits 49-51  matrix base offset (row phase of a start address inside a swizzle repeat)
+//   bits 49-51  matrix base offset (kept 0, see below)
 //   bits 61-63  layout: 0 none, 2 = 128B swizzle, 4 = 64B, 6 = 32B
-__device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t layout, uint32_t sbo_bytes,
-                                              uint32_t base_mode) {
+// The swizzle XOR is taken from the absolute shared-memory address bits, the same rule
+// the TMA unit uses when it writes a 1024-byte-aligned tile. A matrix may therefore
+// start at any 16-byte granule of a swizzled tile (a K step inside a row, or a whole
+// pixel row further down for the next horizontal conv tap) with the base offset left
+// at 0. Verified on B200: a base offset of (start >> 7) & 7 gives wrong products for
+// row-shifted starts, 0 gives exact ones.
+__device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t layout, uint32_t sbo_bytes) {
   uint64_t d = 0;
   d |= static_cast<uint64_t>((saddr & 0x3FFFFu) >> 4);
   d |= static_cast<uint64_t>(1u) << 16;
   d |= static_cast<uint64_t>((sbo_bytes >> 4) & 0x3FFFu) << 32;
   d |= static_cast<uint64_t>(1u) << 46;
-  const uint32_t base_off = base_mode ? ((saddr >> 7) & 7u) : 0u;
-  d |= static_cast<uint64_t>(base_off) << 49;
   d |= static_cast<uint64_t>(layout & 7u) << 61;
   return d;
 }

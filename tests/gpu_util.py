@@ -4,7 +4,7 @@ from __future__ import annotations
 
 import numpy as np
 
-#: BASELINE parity bar for fp16 frame outputs in [0,1]-scale: max-abs and PSNR (peak 1.0).
+#: BASELINE parity bar, defined on the [0,1] output: max-abs and PSNR (peak 1.0).
 MAX_ABS_TOL = 4e-3
 PSNR_MIN_DB = 55.0
 
@@ -15,21 +15,53 @@ def ulp16(v: np.ndarray) -> np.ndarray:
     return 2.0 ** (np.floor(np.log2(a)) - 10)
 
 
-def assert_fp16_layer_close(got: np.ndarray, ref: np.ndarray, label: str, max_ulps: float = 2.0,
-                            min_exact: float = 0.98) -> None:
-    """A single fused layer against its fp32 reference rounded the same way: differences
-    come only from accumulation order flipping an fp16 rounding, so every element must be
-    within `max_ulps` fp16 ulps and nearly all must match exactly."""
+def assert_fp16_layer_close(got: np.ndarray, ref: np.ndarray, label: str, scale: np.ndarray | None = None,
+                            min_exact: float = 0.99) -> None:
+    """One fused layer against an fp32 reference that applies the same fp16 roundings.
+
+    Both compute the conv in fp32 with different summation orders (errors ~1e-6 of the
+    sum of |terms|), so an element may land on the other side of an fp16 rounding
+    boundary: allow one fp16 ulp of the largest intermediate magnitude (`scale`, default
+    |ref|; with residual adds |ref| + sum |adds|), doubled for the cascade through the
+    adds, plus 1e-4 absolute; nearly every element must match exactly."""
     got = got.astype(np.float64)
     ref = ref.astype(np.float64)
     assert got.shape == ref.shape, f"{label}: shape {got.shape} vs {ref.shape}"
     assert np.isfinite(got).all(), f"{label}: non-finite output"
+    s = np.abs(ref) if scale is None else np.maximum(np.abs(ref), scale)
     d = np.abs(got - ref)
-    lim = max_ulps * ulp16(ref) + 1e-7
-    worst = float((d / lim).max())
-    assert worst <= 1.0, f"{label}: max diff {d.max():.3g} ({worst * max_ulps:.2f} ulp)"
+    lim = 2.0 * ulp16(s) + 1e-4
+    bad = d > lim
+    assert not bad.any(), (f"{label}: {int(bad.sum())} elements beyond tolerance; max diff {d.max():.3g}"
+                           f" at |ref|={np.abs(ref).flat[int(np.argmax(d))]:.3g}")
     exact = float((d == 0).mean())
     assert exact >= min_exact, f"{label}: only {exact:.4f} of elements exact"
+
+
+def assert_frame_parity(got: np.ndarray, ref: np.ndarray, label: str) -> tuple[float, float]:
+    """BASELINE's bar for a frame: max-abs <= 4e-3 and PSNR >= 55 dB on the [0,1] output.
+
+    The synthetic ReLU configs end without a Clip and span about [-7, 7], where one fp16
+    ulp is 3.9e-3; there the bar is applied to the [0,1]-clipped frame (what the metric
+    is defined on), and the full range is checked relative to magnitude: every element
+    within 4e-3 * max(1, |ref|), PSNR >= 55 dB with the frame's own peak."""
+    got = got.astype(np.float64)
+    ref = ref.astype(np.float64)
+    assert got.shape == ref.shape, f"{label}: shape {got.shape} vs {ref.shape}"
+    assert np.isfinite(got).all(), f"{label}: non-finite output"
+    gc, rc = np.clip(got, 0, 1), np.clip(ref, 0, 1)
+    d01 = float(np.abs(gc - rc).max())
+    mse01 = float(np.mean((gc - rc) ** 2))
+    psnr01 = float("inf") if mse01 == 0 else 10 * np.log10(1.0 / mse01)
+    assert d01 <= MAX_ABS_TOL, f"{label}: [0,1] max abs diff {d01:.4g} > {MAX_ABS_TOL}"
+    assert psnr01 >= PSNR_MIN_DB, f"{label}: [0,1] PSNR {psnr01:.2f} dB < {PSNR_MIN_DB}"
+    rel = np.abs(got - ref) / np.maximum(1.0, np.abs(ref))
+    assert float(rel.max()) <= MAX_ABS_TOL, f"{label}: full-range relative diff {rel.max():.4g}"
+    peak = float(np.abs(ref).max()) or 1.0
+    mse = float(np.mean((got - ref) ** 2))
+    psnr = float("inf") if mse == 0 else 10 * np.log10(peak * peak / mse)
+    assert psnr >= PSNR_MIN_DB, f"{label}: full-range PSNR {psnr:.2f} dB"
+    return d01, psnr01
 
 
 def torch_conv_layer(x_nhwc, w_oihw, bias, act, adds):

@@ -15,7 +15,7 @@ import pytest
 
 from arthip_b200 import modelgen, onnx_proto as op
 from arthip_b200.engine import Engine
-from gpu_util import MAX_ABS_TOL, PSNR_MIN_DB
+from gpu_util import assert_frame_parity
 from oracle import onnx_cpu
 
 pytestmark = pytest.mark.gpu
@@ -29,12 +29,7 @@ def _model(tmp_path, cfg, seed):
 
 
 def _check(got, ref, label):
-    diff = float(np.abs(got - ref).max())
-    ps = onnx_cpu.psnr(got, ref)
-    assert np.isfinite(got).all(), label
-    assert diff <= MAX_ABS_TOL, f"{label}: max abs diff {diff:.4g}"
-    assert ps >= PSNR_MIN_DB, f"{label}: PSNR {ps:.2f} dB"
-    return diff, ps
+    return assert_frame_parity(got, ref, label)
 
 
 @pytest.mark.parametrize("cfg,seed,h,w", [("C4F32", 0, 256, 256), ("R8F64", 2, 96, 160), ("R16F96", 3, 64, 136)])
