@@ -105,7 +105,7 @@ __global__ void __launch_bounds__(kSimtThreads) conv3x3_simt_kernel(const SimtAr
     if (a.act == kActRelu) {
       t = fmaxf(t, 0.f);
     } else if (a.act == kActSilu) {
-      const float s = r16(1.f / (1.f + __expf(-t)));
+      const float s = r16(1.f / (1.f + expf(-t)));
       t = r16(t * s);
     }
     if (a.add1) t = r16(t + __half2float(a.add1[obase + j]));

@@ -46,6 +46,8 @@ constexpr int kEpiWarps = 8;
 constexpr int kThreads = 64 + 32 * kEpiWarps;
 constexpr int kSmemLimit = 232448;  // 227 KB opt-in dynamic shared memory per block
 constexpr int kStageTile = 2048;    // one 32-pixel x 32-channel fp16 staging tile
+constexpr int kMaxKSteps = 24;      // K steps per kernel row ky: 3 taps x (C/16 <= 8) blocks
+constexpr int kTailBytes = 2048;    // barriers, flags and descriptor tables
 
 struct ConvTcArgs {
   CUtensorMap maps[kTcMaxChunks];
@@ -122,8 +124,8 @@ __device__ __forceinline__ void epilogue8(uint32_t (&h)[4], int act, const __hal
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       const float2 t = __half22float2(*reinterpret_cast<__half2*>(&h[i]));
-      const float s0 = r16(1.f / (1.f + __expf(-t.x)));
-      const float s1 = r16(1.f / (1.f + __expf(-t.y)));
+      const float s0 = r16(1.f / (1.f + expf(-t.x)));
+      const float s1 = r16(1.f / (1.f + expf(-t.y)));
       __half2 o = __floats2half2_rn(t.x * s0, t.y * s1);
       h[i] = *reinterpret_cast<uint32_t*>(&o);
     }
@@ -156,6 +158,10 @@ __global__ void __launch_bounds__(kThreads, 1) conv3x3_tc_kernel(const __grid_co
   uint64_t* donebar = wbar + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(donebar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  // Descriptor tables: per-tap A descriptors relative to slot 0 and B descriptors, so the
+  // MMA issue loop is a table load and an add per instruction.
+  uint64_t* atab = reinterpret_cast<uint64_t*>(bars + 32);
+  uint64_t* btab = atab + kMaxKSteps;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -254,6 +260,21 @@ __global__ void __launch_bounds__(kThreads, 1) conv3x3_tc_kernel(const __grid_co
       const uint32_t sW_u = ptx::smem_u32(sW);
       const uint64_t ones_desc = ptx::smem_desc(ptx::smem_u32(sOnes), 6, 256);
       const uint64_t biasb_desc = ptx::smem_desc(ptx::smem_u32(sBiasB), 6, 256);
+      // K steps of one kernel row (ky): chunk-major, then kx, then 16-channel block.
+      // A descriptors are built for slot 0; another slot is a constant added to the
+      // 14-bit start-address field (every shared address is below 256 KB, so no carry).
+      int KS = 0;
+      for (int k = 0; k < a.nchunks; ++k) {
+        const uint32_t rb = a.rowbytes[k], lay = a.layout[k], sbo = 8u * rb;
+        for (int kx = 0; kx < 3; ++kx)
+          for (int kb = 0; kb < a.kblocks[k]; ++kb, ++KS) {
+            atab[KS] = ptx::smem_desc(sA_u + a.slot_off[k] + kx * rb + kb * 32u, lay, sbo);
+            for (int ky = 0; ky < 3; ++ky)
+              btab[ky * kMaxKSteps + KS] = ptx::smem_desc(sW_u + a.wofs[(ky * 3 + kx) * a.nchunks + k] + kb * 32u,
+                                                          lay, sbo);
+          }
+      }
+      const uint64_t slot_step = static_cast<uint64_t>(a.slot_bytes >> 4);
       bool ok = ptx::mbar_wait(ptx::smem_u32(wbar), 0, abort_flag);
       uint32_t g_base = 0, acc_cnt = 0;
       SegIter it{t0, t1, a.H};
@@ -261,9 +282,11 @@ __global__ void __launch_bounds__(kThreads, 1) conv3x3_tc_kernel(const __grid_co
       while (ok && it.next(sg)) {
         const int n = sg.yb - sg.ya;
         for (int i = 0; i < n && ok; ++i) {
+          uint32_t slot[3];
           for (int ky = 0; ky < 3 && ok; ++ky) {
             const uint32_t gl = g_base + i + ky;
-            ok = ptx::mbar_wait(ptx::smem_u32(&full[gl % S]), (gl / S) & 1u, abort_flag);
+            slot[ky] = gl % S;
+            ok = ptx::mbar_wait(ptx::smem_u32(&full[slot[ky]]), (gl / S) & 1u, abort_flag);
           }
           const uint32_t acc = acc_cnt % NACC;
           if (ok) ok = ptx::mbar_wait(ptx::smem_u32(&acce[acc]), ((acc_cnt / NACC) & 1u) ^ 1u, abort_flag);
@@ -271,25 +294,15 @@ __global__ void __launch_bounds__(kThreads, 1) conv3x3_tc_kernel(const __grid_co
           ptx::tc_fence_after();
           const uint32_t d = tmem_base + acc * a.acc_stride;
           ptx::mma_f16_ss(d, ones_desc, biasb_desc, idesc, 0);  // D = bias
+#pragma unroll 1
           for (int ky = 0; ky < 3; ++ky) {
-            const uint32_t a_slot = sA_u + ((g_base + i + ky) % S) * a.slot_bytes;
-            for (int k = 0; k < a.nchunks; ++k) {
-              const uint32_t rb = a.rowbytes[k];
-              const uint32_t lay = a.layout[k];
-              const uint32_t sbo = 8u * rb;
-              const uint32_t a_chunk = a_slot + a.slot_off[k];
-              for (int kx = 0; kx < 3; ++kx) {
-                const uint32_t b_blk = sW_u + a.wofs[(ky * 3 + kx) * a.nchunks + k];
-                for (int kb = 0; kb < a.kblocks[k]; ++kb) {
-                  const uint64_t ad = ptx::smem_desc(a_chunk + kx * rb + kb * 32u, lay, sbo);
-                  const uint64_t bd = ptx::smem_desc(b_blk + kb * 32u, lay, sbo);
-                  ptx::mma_f16_ss(d, ad, bd, idesc, 1);
-                }
-              }
-            }
+            const uint64_t soff = slot[ky] * slot_step;
+            const uint64_t* bt = btab + ky * kMaxKSteps;
+#pragma unroll 4
+            for (int j = 0; j < KS; ++j) ptx::mma_f16_ss(d, atab[j] + soff, bt[j], idesc, 1);
           }
           ptx::mma_commit(ptx::smem_u32(&accf[acc]));
-          ptx::mma_commit(ptx::smem_u32(&empty[(g_base + i) % S]));
+          ptx::mma_commit(ptx::smem_u32(&empty[slot[0]]));
           ++acc_cnt;
         }
         if (!ok) break;
@@ -335,6 +348,11 @@ __global__ void __launch_bounds__(kThreads, 1) conv3x3_tc_kernel(const __grid_co
           __syncwarp();
         }
         const size_t pix = static_cast<size_t>(y) * a.W + (valid ? x : 0);
+        if (half >= ngroups) {  // no channel group for this warp (MT <= 32): just release
+          ptx::tc_fence_before();
+          __syncwarp();
+          if (lane == 0) ptx::mbar_arrive(ptx::smem_u32(&acce[acc]));
+        }
         for (int g = half, k = 0; g < ngroups; g += 2, ++k) {
           const int cw = min(32, a.MT - g * 32);
           uint32_t rr[32];
@@ -376,7 +394,7 @@ __global__ void __launch_bounds__(kThreads, 1) conv3x3_tc_kernel(const __grid_co
               if (j >= cw || m >= a.M) break;
               float t = r16(__uint_as_float(rr[j]));
               if (a.act == kActRelu) t = fmaxf(t, 0.f);
-              else if (a.act == kActSilu) t = r16(t * r16(1.f / (1.f + __expf(-t))));
+              else if (a.act == kActSilu) t = r16(t * r16(1.f / (1.f + expf(-t))));
               if (a.add1) t = r16(t + __half2float(a.add1[pix * a.M + m]));
               if (a.add2) t = r16(t + __half2float(a.add2[pix * a.M + m]));
               if (o.clip) t = fminf(fmaxf(t, o.clip_lo), o.clip_hi);
@@ -569,7 +587,7 @@ bool conv_tc_plan(const ConvTcWeights* w, const __half* in, int H, int W, const 
   int slot_bytes = 0;
   for (int k = 0; k < w->nchunks; ++k) slot_bytes += w->chunk[k].area;
   P->slot_bytes = slot_bytes;
-  const int fixed = 1024 /*align slack*/ + 4096 /*ones tile*/ + 512 /*barriers + flags*/;
+  const int fixed = 1024 /*align slack*/ + 4096 /*ones tile*/ + kTailBytes;
   // Largest channel slice (divisor of Mpad, multiple of 16) whose weights, bias tile,
   // staging tiles and >= 4 input-row slots fit in shared memory (3 is the minimum).
   int chosen = 0, slots = 0;
@@ -618,7 +636,7 @@ bool conv_tc_plan(const ConvTcWeights* w, const __half* in, int H, int W, const 
   const int ngroups = (chosen + 31) / 32;
   P->stage_per_warp = out.mode == 0 ? ((ngroups + 1) / 2) * kStageTile : 0;
   off += kEpiWarps * P->stage_per_warp;
-  P->smem_bytes = static_cast<size_t>(off) + 512 + 1024;
+  P->smem_bytes = static_cast<size_t>(off) + kTailBytes + 1024;
   P->acc_stride = round_up(chosen, 32);
   P->nacc = (4 * P->acc_stride <= 512) ? 4 : 2;
   int cols = 32;

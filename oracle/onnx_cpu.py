@@ -108,11 +108,14 @@ def _conv_pads(node: op.Node, kh: int, kw: int):
 
 
 class _Exec:
-    def __init__(self, mode: str, use_torch: bool, device: str = "cpu"):
+    def __init__(self, mode: str, use_torch: bool, device: str = "cpu", reverse_channels: bool = False):
         assert mode in ("fp16_nodes", "fp32_nodes", "float64")
         self.mode = mode
         self.use_torch = use_torch and torch is not None and mode != "float64"
         self.device = device
+        # Same arithmetic, different fp32 summation order: measures how far two equally
+        # valid fp16-per-node executions drift apart through a deep chain.
+        self.reverse_channels = reverse_channels
         if self.use_torch and device != "cpu":
             # a reference must not silently drop to TF32 inside cuDNN
             torch.backends.cudnn.allow_tf32 = False
@@ -138,6 +141,8 @@ class _Exec:
         if self.use_torch:
             top, left, bottom, right = pads
             xp = F.pad(x, (left, right, top, bottom))
+            if self.reverse_channels:
+                return F.conv2d(xp.flip(1), w.flip(1), b)
             return F.conv2d(xp, w, b)
         if self.mode == "float64":
             return conv3x3_nchw(x, w, b, pads)
@@ -151,14 +156,14 @@ class _Exec:
 
 def run_model(model: op.Model, x_nchw: np.ndarray, *, mode: str = "fp16_nodes",
               use_torch: bool = True, convert_fp32_weights_to_fp16: bool = False,
-              threads: int | None = None, device: str = "cpu") -> np.ndarray:
+              threads: int | None = None, device: str = "cpu", reverse_channels: bool = False) -> np.ndarray:
     """Execute ``model`` on one NCHW input and return the graph output as float64.
 
     ``convert_fp32_weights_to_fp16`` reproduces the fp16 conversion the engine applies
     to fp32 initializers (IEEE round-to-nearest-even, ``hip_engine.cc:1190-1232``), so
     an fp32-weight model can be compared with the fp16 engine on equal weights."""
     g = model.graph
-    ex = _Exec(mode, use_torch, device)
+    ex = _Exec(mode, use_torch, device, reverse_channels)
     if threads is not None and ex.use_torch:
         torch.set_num_threads(int(threads))
     inits = {t.name: t.to_numpy() for t in g.initializers}

@@ -16,7 +16,7 @@ def ulp16(v: np.ndarray) -> np.ndarray:
 
 
 def assert_fp16_layer_close(got: np.ndarray, ref: np.ndarray, label: str, scale: np.ndarray | None = None,
-                            min_exact: float = 0.99) -> None:
+                            min_exact: float = 0.99, ulps: float = 2.0) -> None:
     """One fused layer against an fp32 reference that applies the same fp16 roundings.
 
     Both compute the conv in fp32 with different summation orders (errors ~1e-6 of the
@@ -30,7 +30,7 @@ def assert_fp16_layer_close(got: np.ndarray, ref: np.ndarray, label: str, scale:
     assert np.isfinite(got).all(), f"{label}: non-finite output"
     s = np.abs(ref) if scale is None else np.maximum(np.abs(ref), scale)
     d = np.abs(got - ref)
-    lim = 2.0 * ulp16(s) + 1e-4
+    lim = ulps * ulp16(s) + 1e-4
     bad = d > lim
     assert not bad.any(), (f"{label}: {int(bad.sum())} elements beyond tolerance; max diff {d.max():.3g}"
                            f" at |ref|={np.abs(ref).flat[int(np.argmax(d))]:.3g}")
@@ -38,7 +38,7 @@ def assert_fp16_layer_close(got: np.ndarray, ref: np.ndarray, label: str, scale:
     assert exact >= min_exact, f"{label}: only {exact:.4f} of elements exact"
 
 
-def assert_frame_parity(got: np.ndarray, ref: np.ndarray, label: str) -> tuple[float, float]:
+def assert_frame_parity(got: np.ndarray, ref: np.ndarray, label: str, tol: float | None = None) -> tuple[float, float]:
     """BASELINE's bar for a frame: max-abs <= 4e-3 and PSNR >= 55 dB on the [0,1] output.
 
     The synthetic ReLU configs end without a Clip and span about [-7, 7], where one fp16
@@ -49,14 +49,15 @@ def assert_frame_parity(got: np.ndarray, ref: np.ndarray, label: str) -> tuple[f
     ref = ref.astype(np.float64)
     assert got.shape == ref.shape, f"{label}: shape {got.shape} vs {ref.shape}"
     assert np.isfinite(got).all(), f"{label}: non-finite output"
+    tol = MAX_ABS_TOL if tol is None else tol
     gc, rc = np.clip(got, 0, 1), np.clip(ref, 0, 1)
     d01 = float(np.abs(gc - rc).max())
     mse01 = float(np.mean((gc - rc) ** 2))
     psnr01 = float("inf") if mse01 == 0 else 10 * np.log10(1.0 / mse01)
-    assert d01 <= MAX_ABS_TOL, f"{label}: [0,1] max abs diff {d01:.4g} > {MAX_ABS_TOL}"
+    assert d01 <= tol, f"{label}: [0,1] max abs diff {d01:.4g} > {tol:.4g}"
     assert psnr01 >= PSNR_MIN_DB, f"{label}: [0,1] PSNR {psnr01:.2f} dB < {PSNR_MIN_DB}"
     rel = np.abs(got - ref) / np.maximum(1.0, np.abs(ref))
-    assert float(rel.max()) <= MAX_ABS_TOL, f"{label}: full-range relative diff {rel.max():.4g}"
+    assert float(rel.max()) <= max(tol, 2.0 ** -8), f"{label}: full-range relative diff {rel.max():.4g}"
     peak = float(np.abs(ref).max()) or 1.0
     mse = float(np.mean((got - ref) ** 2))
     psnr = float("inf") if mse == 0 else 10 * np.log10(peak * peak / mse)

@@ -59,7 +59,10 @@ TC_CASES = [
 def test_tensor_core_conv_matches_fp32_reference(C, M, H, W, act, nadds):
     kind, got, ref, scale = _case(C, M, H, W, act, nadds, seed=C * 1000 + M + H)
     assert kind == "conv_tc"
-    assert_fp16_layer_close(got, ref, f"tc C{C} M{M} {H}x{W} act{act} adds{nadds}", scale)
+    # SiLU rounds the sigmoid to fp16 before the product: a one-ulp sigmoid difference
+    # (fp32 exp error near a rounding boundary) moves the product by up to one more ulp.
+    assert_fp16_layer_close(got, ref, f"tc C{C} M{M} {H}x{W} act{act} adds{nadds}", scale,
+                            ulps=3.0 if act == 2 else 2.0)
 
 
 SIMT_CASES = [
