@@ -46,8 +46,7 @@ constexpr int kEpiWarps = 8;
 constexpr int kThreads = 64 + 32 * kEpiWarps;
 constexpr int kSmemLimit = 232448;  // 227 KB opt-in dynamic shared memory per block
 constexpr int kStageTile = 2048;    // one 32-pixel x 32-channel fp16 staging tile
-constexpr int kMaxKSteps = 24;      // K steps per kernel row ky: 3 taps x (C/16 <= 8) blocks
-constexpr int kTailBytes = 2048;    // barriers, flags and descriptor tables
+constexpr int kTailBytes = 1024;    // barriers and flags
 
 struct ConvTcArgs {
   CUtensorMap maps[kTcMaxChunks];
@@ -141,7 +140,26 @@ __device__ __forceinline__ void epilogue8(uint32_t (&h)[4], int act, const __hal
   if (a2) hadd8(h, a2);
 }
 
+// Compile-time geometry of the input-channel chunks (64-channel chunks first, then at most
+// one 32 and one 16, matching make_chunks on the host). The MMA issue loop is fully
+// unrolled over it, so every descriptor is a register plus a constant: a single issuing
+// thread keeps the tensor core fed (runtime-computed descriptors cost 77-120 cycles per
+// MMA on B200, above the 48-cycle execution time of a 128x64x16 MMA).
+template <int NC64, int NC32, int NC16>
+struct ChunkCfg {
+  static constexpr int N = NC64 + NC32 + NC16;
+  static constexpr int C = 64 * NC64 + 32 * NC32 + 16 * NC16;
+  __host__ __device__ static constexpr int rb(int k) { return k < NC64 ? 128 : (k < NC64 + NC32 ? 64 : 32); }
+  __host__ __device__ static constexpr int kblocks(int k) { return rb(k) / 32; }
+  __host__ __device__ static constexpr uint32_t layout(int k) { return rb(k) == 128 ? 2u : (rb(k) == 64 ? 4u : 6u); }
+  __host__ __device__ static constexpr int area(int k) { return (136 * rb(k) + 1023) / 1024 * 1024; }
+  __host__ __device__ static constexpr int off(int k) { return k == 0 ? 0 : off(k - 1) + area(k - 1); }
+  __host__ __device__ static constexpr uint32_t hi(int k) { return ptx::desc_hi(8u * rb(k), layout(k)); }
+};
+
+template <int NC64, int NC32, int NC16>
 __global__ void __launch_bounds__(kThreads, 1) conv3x3_tc_kernel(const __grid_constant__ ConvTcArgs a) {
+  using Cfg = ChunkCfg<NC64, NC32, NC16>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sW = smem;
@@ -158,10 +176,6 @@ __global__ void __launch_bounds__(kThreads, 1) conv3x3_tc_kernel(const __grid_co
   uint64_t* donebar = wbar + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(donebar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  // Descriptor tables: per-tap A descriptors relative to slot 0 and B descriptors, so the
-  // MMA issue loop is a table load and an add per instruction.
-  uint64_t* atab = reinterpret_cast<uint64_t*>(bars + 32);
-  uint64_t* btab = atab + kMaxKSteps;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -260,49 +274,54 @@ __global__ void __launch_bounds__(kThreads, 1) conv3x3_tc_kernel(const __grid_co
       const uint32_t sW_u = ptx::smem_u32(sW);
       const uint64_t ones_desc = ptx::smem_desc(ptx::smem_u32(sOnes), 6, 256);
       const uint64_t biasb_desc = ptx::smem_desc(ptx::smem_u32(sBiasB), 6, 256);
-      // K steps of one kernel row (ky): chunk-major, then kx, then 16-channel block.
-      // A descriptors are built for slot 0; another slot is a constant added to the
-      // 14-bit start-address field (every shared address is below 256 KB, so no carry).
-      int KS = 0;
-      for (int k = 0; k < a.nchunks; ++k) {
-        const uint32_t rb = a.rowbytes[k], lay = a.layout[k], sbo = 8u * rb;
-        for (int kx = 0; kx < 3; ++kx)
-          for (int kb = 0; kb < a.kblocks[k]; ++kb, ++KS) {
-            atab[KS] = ptx::smem_desc(sA_u + a.slot_off[k] + kx * rb + kb * 32u, lay, sbo);
-            for (int ky = 0; ky < 3; ++ky)
-              btab[ky * kMaxKSteps + KS] = ptx::smem_desc(sW_u + a.wofs[(ky * 3 + kx) * a.nchunks + k] + kb * 32u,
-                                                          lay, sbo);
-          }
-      }
-      const uint64_t slot_step = static_cast<uint64_t>(a.slot_bytes >> 4);
+      // Low descriptor words of the weight block of every (tap, chunk); the A operand of
+      // a slot is its base word plus a compile-time offset (all shared addresses are
+      // below 256 KB, so adding to the 14-bit start field never carries).
+      uint32_t blo[9][Cfg::N];
+#pragma unroll
+      for (int t = 0; t < 9; ++t)
+#pragma unroll
+        for (int k = 0; k < Cfg::N; ++k) blo[t][k] = ptx::desc_lo(sW_u + a.wofs[t * Cfg::N + k]);
+      const uint32_t alo0 = ptx::desc_lo(sA_u);
+      const uint32_t slot16 = static_cast<uint32_t>(a.slot_bytes) >> 4;
       bool ok = ptx::mbar_wait(ptx::smem_u32(wbar), 0, abort_flag);
       uint32_t g_base = 0, acc_cnt = 0;
       SegIter it{t0, t1, a.H};
       Segment sg;
       while (ok && it.next(sg)) {
         const int n = sg.yb - sg.ya;
+        uint32_t slot[3];
+        for (int ky = 0; ky < 2 && ok; ++ky) {  // the first two rows of the segment
+          slot[ky] = (g_base + ky) % S;
+          ok = ptx::mbar_wait(ptx::smem_u32(&full[slot[ky]]), ((g_base + ky) / S) & 1u, abort_flag);
+        }
         for (int i = 0; i < n && ok; ++i) {
-          uint32_t slot[3];
-          for (int ky = 0; ky < 3 && ok; ++ky) {
-            const uint32_t gl = g_base + i + ky;
-            slot[ky] = gl % S;
-            ok = ptx::mbar_wait(ptx::smem_u32(&full[slot[ky]]), (gl / S) & 1u, abort_flag);
-          }
+          // rows i and i+1 of the segment were waited for already; wait for row i+2
+          const uint32_t gl = g_base + i + 2;
+          slot[2] = gl % S;
+          ok = ptx::mbar_wait(ptx::smem_u32(&full[slot[2]]), (gl / S) & 1u, abort_flag);
           const uint32_t acc = acc_cnt % NACC;
           if (ok) ok = ptx::mbar_wait(ptx::smem_u32(&acce[acc]), ((acc_cnt / NACC) & 1u) ^ 1u, abort_flag);
           if (!ok) break;
           ptx::tc_fence_after();
           const uint32_t d = tmem_base + acc * a.acc_stride;
           ptx::mma_f16_ss(d, ones_desc, biasb_desc, idesc, 0);  // D = bias
-#pragma unroll 1
+#pragma unroll
           for (int ky = 0; ky < 3; ++ky) {
-            const uint64_t soff = slot[ky] * slot_step;
-            const uint64_t* bt = btab + ky * kMaxKSteps;
-#pragma unroll 4
-            for (int j = 0; j < KS; ++j) ptx::mma_f16_ss(d, atab[j] + soff, bt[j], idesc, 1);
+            const uint32_t sl = alo0 + slot[ky] * slot16;
+#pragma unroll
+            for (int k = 0; k < Cfg::N; ++k)
+#pragma unroll
+              for (int kx = 0; kx < 3; ++kx)
+#pragma unroll
+                for (int kb = 0; kb < Cfg::kblocks(k); ++kb)
+                  ptx::mma_f16_ss_acc(d, sl + ((Cfg::off(k) + kx * Cfg::rb(k) + kb * 32) >> 4), Cfg::hi(k),
+                                      blo[ky * 3 + kx][k] + kb * 2, Cfg::hi(k), idesc);
           }
           ptx::mma_commit(ptx::smem_u32(&accf[acc]));
           ptx::mma_commit(ptx::smem_u32(&empty[slot[0]]));
+          slot[0] = slot[1];
+          slot[1] = slot[2];
           ++acc_cnt;
         }
         if (!ok) break;
@@ -454,6 +473,22 @@ EncodeTiledFn get_encode_fn() {
       fn = reinterpret_cast<EncodeTiledFn>(p);
   }
   return fn;
+}
+
+typedef void (*ConvTcKernel)(ConvTcArgs);
+
+// The instantiation for an input channel count (C % 16 == 0, 16 <= C <= 128).
+ConvTcKernel pick_kernel(int C) {
+  switch (C) {
+    case 16: return conv3x3_tc_kernel<0, 0, 1>;
+    case 32: return conv3x3_tc_kernel<0, 1, 0>;
+    case 48: return conv3x3_tc_kernel<0, 1, 1>;
+    case 64: return conv3x3_tc_kernel<1, 0, 0>;
+    case 80: return conv3x3_tc_kernel<1, 0, 1>;
+    case 96: return conv3x3_tc_kernel<1, 1, 0>;
+    case 112: return conv3x3_tc_kernel<1, 1, 1>;
+    default: return conv3x3_tc_kernel<2, 0, 0>;
+  }
 }
 
 int layout_for(int cw) { return cw == 64 ? 2 : (cw == 32 ? 4 : 6); }
@@ -654,14 +689,14 @@ bool conv_tc_plan(const ConvTcWeights* w, const __half* in, int H, int W, const 
     if (chosen >= 32 && !encode(enc, &P->out_map32, out.ptr, w->M, W, H, 32, 32, err)) return false;
     if (chosen % 32 == 16 && !encode(enc, &P->out_map16, out.ptr, w->M, W, H, 16, 32, err)) return false;
   }
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(conv3x3_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
+  static bool attr_set[9] = {};
+  if (!attr_set[w->C / 16]) {
+    cudaError_t e = cudaFuncSetAttribute(pick_kernel(w->C), cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
     if (e != cudaSuccess) {
       if (err) *err = std::string("cudaFuncSetAttribute failed: ") + cudaGetErrorString(e);
       return false;
     }
-    attr_set = true;
+    attr_set[w->C / 16] = true;
   }
   return true;
 }
@@ -713,7 +748,7 @@ cudaError_t conv_tc_launch(const ConvTcPlan& P, const __half* add1, const __half
   a.acc_stride = P.acc_stride;
   a.tmem_cols = static_cast<uint32_t>(P.tmem_cols);
   dim3 grid(P.grid_x, P.n_msplit);
-  conv3x3_tc_kernel<<<grid, kThreads, P.smem_bytes, stream>>>(a);
+  pick_kernel(w->C)<<<grid, kThreads, P.smem_bytes, stream>>>(a);
   return cudaGetLastError();
 }
 
