@@ -43,13 +43,13 @@ __global__ void __launch_bounds__(kSimtThreads) conv3x3_simt_kernel(const SimtAr
     __syncthreads();
     wsrc = sw;
   }
-  const long long item = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
-  const long long total = static_cast<long long>(a.H) * a.W * a.groups;
-  if (item >= total) return;
-  const int g = static_cast<int>(item % a.groups);
-  const long long pix = item / a.groups;
-  const int y = static_cast<int>(pix / a.W);
-  const int x = static_cast<int>(pix % a.W);
+  // One grid row per image row; 32-bit index math (64-bit division is costly on GPUs).
+  const int item = blockIdx.x * blockDim.x + threadIdx.x;
+  if (item >= a.W * a.groups) return;
+  const int g = item % a.groups;
+  const int x = item / a.groups;
+  const int y = blockIdx.y;
+  const long long pix = static_cast<long long>(y) * a.W + x;
   const int mg0 = g * MG;
   const int nm = min(MG, a.M - mg0);
 
@@ -154,14 +154,11 @@ __global__ void __launch_bounds__(kSimtThreads) conv3x3_simt_kernel(const SimtAr
 
 template <int MG, bool VEC8>
 cudaError_t launch_simt(const SimtArgs& a, size_t smem, cudaStream_t s) {
-  const long long total = static_cast<long long>(a.H) * a.W * a.groups;
-  const long long blocks = (total + kSimtThreads - 1) / kSimtThreads;
-  if (smem > 0) {
-    cudaError_t e = cudaFuncSetAttribute(conv3x3_simt_kernel<MG, VEC8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(smem));
-    if (e != cudaSuccess) return e;
-  }
-  conv3x3_simt_kernel<MG, VEC8><<<static_cast<unsigned>(blocks), kSimtThreads, smem, s>>>(a);
+  // Weights are staged only when they fit the default 48 KB dynamic shared memory, so no
+  // function attribute (and nothing that is not stream-ordered) is needed here.
+  const dim3 grid(static_cast<unsigned>((a.W * a.groups + kSimtThreads - 1) / kSimtThreads),
+                  static_cast<unsigned>(a.H));
+  conv3x3_simt_kernel<MG, VEC8><<<grid, kSimtThreads, smem, s>>>(a);
   return cudaGetLastError();
 }
 

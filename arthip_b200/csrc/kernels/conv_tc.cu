@@ -41,7 +41,7 @@ namespace ah {
 namespace {
 
 constexpr int kMaxSlots = 8;
-constexpr int kMaxAcc = 4;
+constexpr int kMaxAcc = 16;         // accumulator ring entries (16 = vertical mode with M = 32)
 constexpr int kEpiWarps = 8;
 constexpr int kThreads = 64 + 32 * kEpiWarps;
 constexpr int kSmemLimit = 232448;  // 227 KB opt-in dynamic shared memory per block
@@ -75,6 +75,7 @@ struct ConvTcArgs {
   long long rows_total;
   int act;
   int nacc, acc_stride;
+  int vert;     // vertical-window formulation: nacc = 512 / M ring chunks of M columns
   uint32_t tmem_cols;
 };
 
@@ -230,16 +231,16 @@ __global__ void __launch_bounds__(kThreads, 1) conv3x3_tc_kernel(const __grid_co
   if (warp == 0) {
     // ---------------- TMA producer ----------------
     if (lane == 0) {
+      // weight blocks: 9 taps x chunks of MT rows, or (vertical) 3 kx x chunks of 3M rows
+      const int nblk = (a.vert ? 3 : 9) * a.nchunks;
+      const int wrows = a.vert ? 3 * a.MT : a.MT;
       uint32_t wbytes = 0;
-      for (int t = 0; t < 9; ++t)
-        for (int k = 0; k < a.nchunks; ++k) wbytes += a.MT * a.rowbytes[k];
+      for (int idx = 0; idx < nblk; ++idx) wbytes += wrows * a.rowbytes[idx % a.nchunks];
       ptx::mbar_arrive_expect_tx(ptx::smem_u32(wbar), wbytes);
-      for (int t = 0; t < 9; ++t) {
-        for (int k = 0; k < a.nchunks; ++k) {
-          const int idx = t * a.nchunks + k;
-          const uint8_t* src = a.wpack + a.gofs[idx] + static_cast<long long>(m0) * a.rowbytes[k];
-          ptx::bulk_load(ptx::smem_u32(sW + a.wofs[idx]), src, a.MT * a.rowbytes[k], ptx::smem_u32(wbar));
-        }
+      for (int idx = 0; idx < nblk; ++idx) {
+        const int k = idx % a.nchunks;
+        const uint8_t* src = a.wpack + a.gofs[idx] + static_cast<long long>(m0) * a.rowbytes[k];
+        ptx::bulk_load(ptx::smem_u32(sW + a.wofs[idx]), src, wrows * a.rowbytes[k], ptx::smem_u32(wbar));
       }
       uint32_t g = 0;
       SegIter it{t0, t1, a.H};
@@ -288,7 +289,64 @@ __global__ void __launch_bounds__(kThreads, 1) conv3x3_tc_kernel(const __grid_co
       uint32_t g_base = 0, acc_cnt = 0;
       SegIter it{t0, t1, a.H};
       Segment sg;
-      while (ok && it.next(sg)) {
+      if (a.vert) {
+        // Vertical window: input row j of a segment feeds output rows j, j-1, j-2 through
+        // kernel rows ky = 0, 1, 2. Output row o lives in TMEM chunk ring(o) of M columns
+        // (ring(o) = -o mod NCH), so those outputs occupy consecutive chunks and the
+        // three kernel rows (stacked along N in the weight block) go out as one MMA of
+        // N = 3M (split in two where the window wraps around the ring).
+        const uint32_t M = a.MT, NCH = a.nacc;
+        const uint32_t idM = ptx::idesc_f16_f32(kTcTilePx, M);
+        uint32_t bv[3][Cfg::N];
+#pragma unroll
+        for (int kx = 0; kx < 3; ++kx)
+#pragma unroll
+          for (int k = 0; k < Cfg::N; ++k) bv[kx][k] = ptx::desc_lo(sW_u + a.wofs[kx * Cfg::N + k]);
+        uint32_t g = 0, obase = 0;
+        while (ok && it.next(sg)) {
+          const int n = sg.yb - sg.ya;
+          for (int j = 0; j <= n + 1 && ok; ++j, ++g) {
+            const uint32_t slot = g % S;
+            ok = ptx::mbar_wait(ptx::smem_u32(&full[slot]), (g / S) & 1u, abort_flag);
+            const int ky_lo = max(0, j - (n - 1)), ky_hi = min(2, j);
+            if (ok && ky_lo == 0) {  // output row j starts here: bias-initialise its chunk
+              const uint32_t o = obase + j, c = (NCH - (o & (NCH - 1))) & (NCH - 1);
+              ok = ptx::mbar_wait(ptx::smem_u32(&acce[c]), ((o / NCH) & 1u) ^ 1u, abort_flag);
+              ptx::tc_fence_after();
+              if (ok) ptx::mma_f16_ss(tmem_base + c * M, ones_desc, biasb_desc, idM, 0);
+            }
+            if (!ok) break;
+            const uint32_t ohi = obase + j - ky_lo;
+            const uint32_t chi = (NCH - (ohi & (NCH - 1))) & (NCH - 1);
+            const uint32_t span = ky_hi - ky_lo + 1;
+            const uint32_t n1 = min(span, NCH - chi), n2 = span - n1;
+            const uint32_t d1 = tmem_base + chi * M, d2 = tmem_base;
+            const uint32_t i1 = ptx::idesc_f16_f32(kTcTilePx, n1 * M), i2 = ptx::idesc_f16_f32(kTcTilePx, n2 * M);
+            const uint32_t sl = alo0 + slot * slot16;
+#pragma unroll
+            for (int k = 0; k < Cfg::N; ++k) {
+              const uint32_t mrows16 = (M * Cfg::rb(k)) >> 4;  // M weight rows, in 16-byte units
+              const uint32_t b1 = ky_lo * mrows16, b2 = (ky_lo + n1) * mrows16;
+#pragma unroll
+              for (int kx = 0; kx < 3; ++kx)
+#pragma unroll
+                for (int kb = 0; kb < Cfg::kblocks(k); ++kb) {
+                  const uint32_t alo = sl + ((Cfg::off(k) + kx * Cfg::rb(k) + kb * 32) >> 4);
+                  const uint32_t blo = bv[kx][k] + kb * 2;
+                  ptx::mma_f16_ss_acc(d1, alo, Cfg::hi(k), blo + b1, Cfg::hi(k), i1);
+                  if (n2) ptx::mma_f16_ss_acc(d2, alo, Cfg::hi(k), blo + b2, Cfg::hi(k), i2);
+                }
+            }
+            ptx::mma_commit(ptx::smem_u32(&empty[slot]));
+            if (ky_hi == 2) {  // output row j-2 received its last kernel row
+              const uint32_t o = obase + j - 2, c = (NCH - (o & (NCH - 1))) & (NCH - 1);
+              ptx::mma_commit(ptx::smem_u32(&accf[c]));
+            }
+          }
+          obase += n;
+        }
+      }
+      while (ok && !a.vert && it.next(sg)) {
         const int n = sg.yb - sg.ya;
         uint32_t slot[3];
         for (int ky = 0; ky < 2 && ok; ++ky) {  // the first two rows of the segment
@@ -353,7 +411,9 @@ __global__ void __launch_bounds__(kThreads, 1) conv3x3_tc_kernel(const __grid_co
       const int x = xw + lane;
       const bool valid = x < a.W;
       for (int y = sg.ya; y < sg.yb; ++y) {
-        const uint32_t acc = acc_cnt % NACC;
+        // accumulator of this output row: ring position -o mod NACC in the vertical
+        // formulation (consecutive rows in descending chunks), o mod NACC otherwise
+        const uint32_t acc = a.vert ? ((NACC - (acc_cnt & (NACC - 1))) & (NACC - 1)) : (acc_cnt % NACC);
         int w_ok = 0;
         if (lane == 0) w_ok = ptx::mbar_wait(ptx::smem_u32(&accf[acc]), (acc_cnt / NACC) & 1u, abort_flag) ? 1 : 0;
         w_ok = __shfl_sync(0xffffffffu, w_ok, 0);
@@ -550,29 +610,58 @@ bool conv_tc_supported(int C, int M, std::string* why) {
   return true;
 }
 
+namespace {
+
+int slot_bytes_of(const ConvTcWeights* w) {
+  int s = 0;
+  for (int k = 0; k < w->nchunks; ++k) s += w->chunk[k].area;
+  return s;
+}
+
+// Shared memory of a plan: weights + row slots + ones/bias tiles + staging + tail.
+int smem_need(const ConvTcWeights* w, int MT, bool vert, int mode, int slots) {
+  int wb = 0;
+  for (int b = 0; b < (vert ? 3 : 9); ++b)
+    for (int k = 0; k < w->nchunks; ++k) wb += round_up((vert ? 3 : 1) * MT * w->chunk[k].rowbytes, 1024);
+  const int ngroups = (MT + 31) / 32;
+  const int stage = mode == 0 ? kEpiWarps * ((ngroups + 1) / 2) * kStageTile : 0;
+  return wb + slots * slot_bytes_of(w) + 4096 + round_up(MT * 32, 1024) + stage + kTailBytes + 1024;
+}
+
+}  // namespace
+
 std::vector<uint8_t> conv_tc_pack_host(const uint16_t* w_oihw, int C, int M, ConvTcWeights* L) {
   make_chunks(C, L);
   L->C = C;
   L->M = M;
   L->Mpad = round_up(M, 16);
   const int Mp = L->Mpad;
+  // The vertical-window formulation needs M = 32 or 64 (3M <= 256 columns per MMA and
+  // 512/M ring chunks) and its weights plus 3 row slots resident in shared memory.
+  L->vert = ((M == 32 || M == 64) && smem_need(L, M, true, 0, 3) <= kSmemLimit) ? 1 : 0;
+  const int nblk = L->vert ? 3 : 9;
+  const int rows = L->vert ? 3 * M : Mp;
   long long off = 0;
-  for (int t = 0; t < 9; ++t)
+  for (int b = 0; b < nblk; ++b)
     for (int k = 0; k < L->nchunks; ++k) {
-      L->gofs[t * L->nchunks + k] = off;
-      off += static_cast<long long>(Mp) * L->chunk[k].rowbytes;
+      L->gofs[b * L->nchunks + k] = off;
+      off += static_cast<long long>(rows) * L->chunk[k].rowbytes;
     }
   std::vector<uint8_t> img(static_cast<size_t>(off), 0);
-  for (int t = 0; t < 9; ++t) {
+  for (int b = 0; b < nblk; ++b) {
     for (int k = 0; k < L->nchunks; ++k) {
       const ConvTcChunk& ch = L->chunk[k];
-      uint8_t* blk = img.data() + L->gofs[t * L->nchunks + k];
-      for (int m = 0; m < M; ++m)
+      uint8_t* blk = img.data() + L->gofs[b * L->nchunks + k];
+      // standard: block b = tap, row = m; vertical: block b = kx, row = ky * M + m
+      for (int r = 0; r < (L->vert ? 3 * M : M); ++r) {
+        const int m = L->vert ? r % M : r;
+        const int tap = L->vert ? (r / M) * 3 + b : b;
         for (int kk = 0; kk < ch.cw; ++kk) {
           const int c = ch.c0 + kk;
-          const uint16_t v = w_oihw[(static_cast<size_t>(m) * C + c) * 9 + t];
-          std::memcpy(blk + swz_granule(m, (kk * 2) / 16, ch.rowbytes) + (kk * 2) % 16, &v, 2);
+          const uint16_t v = w_oihw[(static_cast<size_t>(m) * C + c) * 9 + tap];
+          std::memcpy(blk + swz_granule(r, (kk * 2) / 16, ch.rowbytes) + (kk * 2) % 16, &v, 2);
         }
+      }
     }
   }
   L->wpack_bytes = img.size();
@@ -619,32 +708,34 @@ bool conv_tc_plan(const ConvTcWeights* w, const __half* in, int H, int W, const 
   P->H = H;
   P->W = W;
   P->out = out;
-  int slot_bytes = 0;
-  for (int k = 0; k < w->nchunks; ++k) slot_bytes += w->chunk[k].area;
+  const int slot_bytes = slot_bytes_of(w);
   P->slot_bytes = slot_bytes;
-  const int fixed = 1024 /*align slack*/ + 4096 /*ones tile*/ + kTailBytes;
-  // Largest channel slice (divisor of Mpad, multiple of 16) whose weights, bias tile,
-  // staging tiles and >= 4 input-row slots fit in shared memory (3 is the minimum).
+  const bool vert = w->vert != 0;
   int chosen = 0, slots = 0;
-  for (int nsplit = 1; nsplit <= w->Mpad / 16 && !chosen; ++nsplit) {
-    if (w->Mpad % nsplit) continue;
-    const int MT = w->Mpad / nsplit;
-    if (MT % 16) continue;
-    int wb = 0;
-    for (int t = 0; t < 9; ++t)
-      for (int k = 0; k < w->nchunks; ++k) wb += round_up(MT * w->chunk[k].rowbytes, 1024);
-    const int ngroups = (MT + 31) / 32;
-    const int stage = out.mode == 0 ? kEpiWarps * ((ngroups + 1) / 2) * kStageTile : 0;
-    const int base = wb + stage + round_up(MT * 32, 1024) + fixed;
-    bool can_split = false;
-    for (int ns = nsplit + 1; ns <= w->Mpad / 16; ++ns)
-      if (w->Mpad % ns == 0 && (w->Mpad / ns) % 16 == 0) can_split = true;
-    for (int s = kMaxSlots; s >= 3; --s) {
-      if (base + s * slot_bytes <= kSmemLimit) {
-        if (s < 4 && can_split) break;  // rather split the channels than run a 3-slot ring
-        chosen = MT;
+  if (vert) {
+    // Whole output-channel range per CTA; deepest input-row ring that fits.
+    for (int s = kMaxSlots; s >= 3 && !chosen; --s)
+      if (smem_need(w, w->M, true, out.mode, s) <= kSmemLimit) {
+        chosen = w->M;
         slots = s;
-        break;
+      }
+  } else {
+    // Largest channel slice (divisor of Mpad, multiple of 16) whose weights, bias tile,
+    // staging tiles and >= 4 input-row slots fit in shared memory (3 is the minimum).
+    for (int nsplit = 1; nsplit <= w->Mpad / 16 && !chosen; ++nsplit) {
+      if (w->Mpad % nsplit) continue;
+      const int MT = w->Mpad / nsplit;
+      if (MT % 16) continue;
+      bool can_split = false;
+      for (int ns = nsplit + 1; ns <= w->Mpad / 16; ++ns)
+        if (w->Mpad % ns == 0 && (w->Mpad / ns) % 16 == 0) can_split = true;
+      for (int s = kMaxSlots; s >= 3; --s) {
+        if (smem_need(w, MT, false, out.mode, s) <= kSmemLimit) {
+          if (s < 4 && can_split) break;  // rather split the channels than run a 3-slot ring
+          chosen = MT;
+          slots = s;
+          break;
+        }
       }
     }
   }
@@ -652,14 +743,15 @@ bool conv_tc_plan(const ConvTcWeights* w, const __half* in, int H, int W, const 
     if (err) *err = "tensor-core conv: weights and row slots do not fit in shared memory";
     return false;
   }
+  P->vert = vert ? 1 : 0;
   P->MT = chosen;
   P->n_msplit = w->Mpad / chosen;
   P->nslots = slots;
   int off = 0;
-  for (int t = 0; t < 9; ++t)
+  for (int b = 0; b < (vert ? 3 : 9); ++b)
     for (int k = 0; k < w->nchunks; ++k) {
-      P->wofs[t * w->nchunks + k] = off;
-      off += round_up(chosen * w->chunk[k].rowbytes, 1024);
+      P->wofs[b * w->nchunks + k] = off;
+      off += round_up((vert ? 3 : 1) * chosen * w->chunk[k].rowbytes, 1024);
     }
   P->w_smem_bytes = off;
   off += slots * slot_bytes;
@@ -672,11 +764,18 @@ bool conv_tc_plan(const ConvTcWeights* w, const __half* in, int H, int W, const 
   P->stage_per_warp = out.mode == 0 ? ((ngroups + 1) / 2) * kStageTile : 0;
   off += kEpiWarps * P->stage_per_warp;
   P->smem_bytes = static_cast<size_t>(off) + kTailBytes + 1024;
-  P->acc_stride = round_up(chosen, 32);
-  P->nacc = (4 * P->acc_stride <= 512) ? 4 : 2;
-  int cols = 32;
-  while (cols < P->nacc * P->acc_stride) cols *= 2;
-  P->tmem_cols = cols;
+  if (vert) {
+    // TMEM as a ring of 512 / M chunks of M columns, one per output row in flight.
+    P->acc_stride = chosen;
+    P->nacc = 512 / chosen;
+    P->tmem_cols = 512;
+  } else {
+    P->acc_stride = round_up(chosen, 32);
+    P->nacc = (4 * P->acc_stride <= 512) ? 4 : 2;
+    int cols = 32;
+    while (cols < P->nacc * P->acc_stride) cols *= 2;
+    P->tmem_cols = cols;
+  }
   const long long n_strips = (W + kTcTilePx - 1) / kTcTilePx;
   const long long rows_total = n_strips * H;
   long long gx = std::max(1, num_sms / P->n_msplit);
@@ -746,6 +845,7 @@ cudaError_t conv_tc_launch(const ConvTcPlan& P, const __half* add1, const __half
   a.act = act;
   a.nacc = P.nacc;
   a.acc_stride = P.acc_stride;
+  a.vert = P.vert;
   a.tmem_cols = static_cast<uint32_t>(P.tmem_cols);
   dim3 grid(P.grid_x, P.n_msplit);
   pick_kernel(w->C)<<<grid, kThreads, P.smem_bytes, stream>>>(a);

@@ -37,9 +37,13 @@ struct ConvTcChunk {
 struct ConvTcWeights {
   int C = 0, M = 0;
   int Mpad = 0;                // M rounded up to 16 (zero weights and bias in the padding)
+  // Vertical-window packing (M = 32 or 64): one block per (kx, chunk) holding the three
+  // kernel rows ky stacked along N (3M rows), so one MMA of N = 3M serves the three
+  // output rows an input row feeds. Otherwise one block of Mpad rows per (tap, chunk).
+  int vert = 0;
   int nchunks = 0;
   ConvTcChunk chunk[kTcMaxChunks];
-  void* wpack = nullptr;       // device: [tap][chunk] blocks of Mpad swizzled rows
+  void* wpack = nullptr;       // device: swizzled K-major weight blocks (see vert)
   size_t wpack_bytes = 0;
   long long gofs[9 * kTcMaxChunks] = {};  // byte offset of each (tap, chunk) block
   float* bias = nullptr;       // device: Mpad fp32 (fp16-rounded values)
@@ -71,6 +75,7 @@ struct ConvTcPlan {
   int ones_off = 0, biasb_off = 0, stage_off = 0, stage_per_warp = 0;
   size_t smem_bytes = 0;
   int nacc = 0, acc_stride = 0, tmem_cols = 0;
+  int vert = 0;                // vertical-window MMA formulation (weights packed accordingly)
   int grid_x = 0;
   ConvTcOut out;
   CUtensorMap maps[kTcMaxChunks];
