@@ -630,32 +630,37 @@ int smem_need(const ConvTcWeights* w, int MT, bool vert, int mode, int slots) {
 
 }  // namespace
 
-std::vector<uint8_t> conv_tc_pack_host(const uint16_t* w_oihw, int C, int M, ConvTcWeights* L) {
+size_t conv_tc_pack_layout(int C, int M, ConvTcWeights* L) {
   make_chunks(C, L);
   L->C = C;
   L->M = M;
   L->Mpad = round_up(M, 16);
-  const int Mp = L->Mpad;
   // The vertical-window formulation needs M = 32 or 64 (3M <= 256 columns per MMA and
   // 512/M ring chunks) and its weights plus 3 row slots resident in shared memory.
   L->vert = ((M == 32 || M == 64) && smem_need(L, M, true, 0, 3) <= kSmemLimit) ? 1 : 0;
   const int nblk = L->vert ? 3 : 9;
-  const int rows = L->vert ? 3 * M : Mp;
+  const int rows = L->vert ? 3 * M : L->Mpad;
   long long off = 0;
   for (int b = 0; b < nblk; ++b)
     for (int k = 0; k < L->nchunks; ++k) {
       L->gofs[b * L->nchunks + k] = off;
       off += static_cast<long long>(rows) * L->chunk[k].rowbytes;
     }
-  std::vector<uint8_t> img(static_cast<size_t>(off), 0);
-  for (int b = 0; b < nblk; ++b) {
-    for (int k = 0; k < L->nchunks; ++k) {
-      const ConvTcChunk& ch = L->chunk[k];
-      uint8_t* blk = img.data() + L->gofs[b * L->nchunks + k];
+  L->wpack_bytes = static_cast<size_t>(off);
+  return L->wpack_bytes;
+}
+
+void conv_tc_pack_into(const uint16_t* w_oihw, const ConvTcWeights& L, uint8_t* img) {
+  std::memset(img, 0, L.wpack_bytes);
+  const int C = L.C, M = L.M;
+  for (int b = 0; b < (L.vert ? 3 : 9); ++b) {
+    for (int k = 0; k < L.nchunks; ++k) {
+      const ConvTcChunk& ch = L.chunk[k];
+      uint8_t* blk = img + L.gofs[b * L.nchunks + k];
       // standard: block b = tap, row = m; vertical: block b = kx, row = ky * M + m
-      for (int r = 0; r < (L->vert ? 3 * M : M); ++r) {
-        const int m = L->vert ? r % M : r;
-        const int tap = L->vert ? (r / M) * 3 + b : b;
+      for (int r = 0; r < (L.vert ? 3 * M : M); ++r) {
+        const int m = L.vert ? r % M : r;
+        const int tap = L.vert ? (r / M) * 3 + b : b;
         for (int kk = 0; kk < ch.cw; ++kk) {
           const int c = ch.c0 + kk;
           const uint16_t v = w_oihw[(static_cast<size_t>(m) * C + c) * 9 + tap];
@@ -664,7 +669,11 @@ std::vector<uint8_t> conv_tc_pack_host(const uint16_t* w_oihw, int C, int M, Con
       }
     }
   }
-  L->wpack_bytes = img.size();
+}
+
+std::vector<uint8_t> conv_tc_pack_host(const uint16_t* w_oihw, int C, int M, ConvTcWeights* L) {
+  std::vector<uint8_t> img(conv_tc_pack_layout(C, M, L));
+  conv_tc_pack_into(w_oihw, *L, img.data());
   return img;
 }
 

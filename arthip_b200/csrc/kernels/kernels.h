@@ -88,7 +88,10 @@ bool conv_tc_supported(int C, int M, std::string* why);
 cudaError_t conv_tc_upload(const uint16_t* w_oihw_f16, const float* bias_or_null, int C, int M,
                            ConvTcWeights* out);
 void conv_tc_free(ConvTcWeights* w);
-// Host-only packing (exposed for tests): returns the packed byte image.
+// Host-only packing: the layout (chunks, block offsets, formulation) and its byte size,
+// then the swizzled image into a caller buffer of that size, or into a new vector.
+size_t conv_tc_pack_layout(int C, int M, ConvTcWeights* layout);
+void conv_tc_pack_into(const uint16_t* w_oihw_f16, const ConvTcWeights& layout, uint8_t* img);
 std::vector<uint8_t> conv_tc_pack_host(const uint16_t* w_oihw_f16, int C, int M, ConvTcWeights* layout);
 // Builds the per-frame plan (tensor maps over `in` and, for mode 0, `out.ptr`).
 // Fails with a message when the tiles cannot fit in shared memory.
