@@ -9,15 +9,18 @@ stream with no collective on the data path ("scaling": "weak"); the barrier and 
 max-over-ranks timing are host plumbing only.
 
 value: frames/s over all ranks, device-resident (inputs already in HBM: a ring of 8
-  synthetic frames copied into the engine's input buffer on its stream each step),
-  timed with CUDA events on the engine stream (first frame start -> last frame end),
-  max over ranks. Activations (265 MB per tensor) exceed the 126 MB L2, so no flush.
+  synthetic frames copied into the engine's input buffer on its stream each step), each
+  frame one replay of the engine's captured CUDA graph; timed with CUDA events on the
+  engine stream around the K frames, max over ranks. Activations (265 MB per tensor)
+  exceed the 126 MB L2, so no flush is needed between frames.
 e2e: the same metric through the public C ABI call ``ah_engine_run`` with pinned host
   buffers: per step an H2D copy of the frame and a D2H copy of the 2x output.
 roofline: the dominant kernel (the tcgen05 conv) as algorithmic direct-conv FLOPs per
-  launch / its mean CUDA-event duration inside the timed region.
+  launch / its mean duration, from a per-op pass right after the timed region that
+  launches the same ops with a CUDA event between consecutive ops (table on stderr).
 --impl reference: the reference's CPU path (ONNX Runtime CPU is not installable here;
-  the oracle's torch-CPU restatement of the same graph) on all host cores.
+  the oracle's torch-CPU restatement of the same graph) on all host cores, one 45-row
+  strip of the frame per step, at most ~100 s of CPU time in total.
 """
 
 from __future__ import annotations
@@ -148,20 +151,23 @@ def build_model(tmpdir: Path):
     return cm, p
 
 
-def cpu_reference_fps(cm, rows: int, reps: int, threads: int):
+def cpu_reference_fps(cm, rows: int, reps: int, threads: int, budget_s: float = 30.0):
     """The oracle's torch-CPU restatement of the graph on a horizontal strip of the frame;
-    fps scales by 1080/rows (conv cost is linear in pixels)."""
+    fps scales by 1080/rows (conv cost is linear in pixels). Stops after `reps` strips or
+    once `budget_s` seconds of strips have run, whichever comes first."""
     from arthip_b200 import modelgen
     from oracle import onnx_cpu
     x = modelgen.synthetic_frame(SEED, 1, rows, W).astype(np.float64)
     onnx_cpu.run_model(cm.model, x[:, :, : max(8, rows // 8)], mode="fp32_nodes", threads=threads)  # warm
     times = []
-    for _ in range(reps):
+    t_start = time.perf_counter()
+    while len(times) < reps and (not times or time.perf_counter() - t_start < budget_s):
         t0 = time.perf_counter()
         onnx_cpu.run_model(cm.model, x, mode="fp32_nodes", threads=threads)
         times.append(time.perf_counter() - t0)
     per_frame = statistics.median(times) * (H / rows)
-    return 1.0 / per_frame, f"{rows}x{W} strip of the 1080p frame x{reps} (median), scaled by {H}/{rows}"
+    return 1.0 / per_frame, (f"{rows}x{W} strip of the 1080p frame x{len(times)} (median), scaled by {H}/{rows}; "
+                             f"{threads} torch threads")
 
 
 def run_reference(args):
@@ -173,7 +179,7 @@ def run_reference(args):
     with tempfile.TemporaryDirectory() as td:
         cm, _ = build_model(Path(td))
         rows = 45
-        fps, sample = cpu_reference_fps(cm, rows, max(1, args.steps), threads)
+        fps, sample = cpu_reference_fps(cm, rows, max(1, args.steps), threads, budget_s=100.0)
     line = {"impl": "reference", "metric": METRIC, "value": fps, "unit": UNIT, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 / fps, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
@@ -247,17 +253,30 @@ def main():
         except Exception:
             pass
 
+        # -------- timed region: K frames through the captured CUDA graph --------
         dist_barrier(world)
         torch.cuda.synchronize()
-        eng.timing_start(args.steps)
+        ev0 = torch.cuda.Event(enable_timing=True)
+        ev1 = torch.cuda.Event(enable_timing=True)
         with ClockSampler(gpu_uuid) as clk:
+            ev0.record(estream)
             for i in range(args.steps):
                 step(i)
-            op_ms, span_ms, frames = eng.timing_read()
-        torch.cuda.synchronize()
+            ev1.record(estream)
+            eng.synchronize()
+            torch.cuda.synchronize()
         dist_barrier(world)
-        span_max = dist_max(span_ms, world)
+        span_max = dist_max(ev0.elapsed_time(ev1), world)
+        frames = args.steps
         clocks = clk.summary()
+
+        # -------- per-op pass: the same launches with a CUDA event between ops --------
+        op_frames = max(3, min(args.steps, 50))
+        eng.timing_start(op_frames)
+        for i in range(op_frames):
+            step(i)
+        op_ms, _, op_count = eng.timing_read()
+        op_ms = [t / op_count for t in op_ms]
 
         # -------- e2e: public C-ABI call with pinned host buffers --------
         e2e_steps = args.e2e_steps or max(10, min(args.steps, 200))
@@ -279,15 +298,24 @@ def main():
         return 0
 
     fps = world * frames / (span_max / 1000.0)
-    # roofline of the dominant kernel: all tcgen05 conv launches
-    tc = [(o, t / frames) for o, t in zip(ops, op_ms) if o["kind"] == "conv_tc"]
+    # roofline of the dominant kernel: all tcgen05 conv launches of a frame
+    tc = [(o, t) for o, t in zip(ops, op_ms) if o["kind"] == "conv_tc"]
     tc_flops = sum(o["flops"] for o, _ in tc)
     tc_ms = sum(t for _, t in tc)
     achieved_tflops = tc_flops / (tc_ms / 1e3) / 1e12 if tc_ms > 0 else 0.0
     peak_tf = peaks.get("bf16_tflops_sustained", peaks.get("bf16_tflops"))
     frame_ms = span_max / frames
-    roof_ms = sum(max(o["flops"] / (peaks["bf16_tflops"] * 1e12), o["bytes"] / (peaks["hbm_gbs"] * 1e9)) * 1e3
-                  for o in ops)
+    roof = [max(o["flops"] / (peaks["bf16_tflops"] * 1e12), o["bytes"] / (peaks["hbm_gbs"] * 1e9)) * 1e3
+            for o in ops]
+    roof_ms = sum(roof)
+    print(f"{'op':>3} {'kind':<10} {'ms':>8} {'roof_ms':>8} {'frac':>6} {'TFLOP/s':>8} {'GB/s':>8}  label",
+          file=sys.stderr)
+    for i, (o, t, r) in enumerate(zip(ops, op_ms, roof)):
+        print(f"{i:>3} {o['kind']:<10} {t:8.4f} {r:8.4f} {r / t if t else 0:6.3f} "
+              f"{o['flops'] / t / 1e9 if t else 0:8.1f} {o['bytes'] / t / 1e6 if t else 0:8.1f}  {o['label']}",
+              file=sys.stderr)
+    print(f"sum of ops {sum(op_ms):.4f} ms/frame (events between ops); graph path {frame_ms:.4f} ms/frame",
+          file=sys.stderr)
     traffic = None
     tp = ROOT / "profiles" / "conv_tc_traffic.json"
     if tp.exists():
@@ -327,6 +355,8 @@ def main():
                      "frame_roofline_frac": roof_ms / frame_ms, "frame_roofline_ms": roof_ms},
         "kernel_share": {k: v / tot for k, v in share.items()},
         "gpu_launches": frames * len(ops),
+        "op_pass": {"frames": op_count, "ms_per_frame": sum(op_ms),
+                    "note": "per-op CUDA events in a pass right after the timed region; roofline uses it"},
         "cpu_baseline": cpu,
     }
     print(json.dumps(line))
