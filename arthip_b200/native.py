@@ -47,6 +47,8 @@ SIGNATURES: dict[str, tuple] = {
     "ah_conv3x3_kind": (_i32, [_vp]),
     "ah_conv3x3_status": (_i32, [_vp, _u32p]),
     "ah_conv3x3_destroy": (None, [_vp]),
+    "ah_conv3x3_run_noalloc": (_i32, [_i32, _i32, _i32, _vp, _vp, _i32, _vp, _i32, _i32, _vp, _vp, _vp, _vp,
+                                      _cp, _i32]),
     "ah_float_to_half_rne": (None, [_vp, _vp, _sz]),
     "ah_float_to_half_ftz": (None, [_vp, _vp, _sz]),
     "ah_half_to_float": (None, [_vp, _vp, _sz]),

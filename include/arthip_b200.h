@@ -116,6 +116,22 @@ int ah_conv3x3_kind(ah_conv* c);
 int ah_conv3x3_status(ah_conv* c, uint32_t* status);
 void ah_conv3x3_destroy(ah_conv* c);
 
+/* Allocation-free single conv layer (no counterpart in the reference; an addition of this
+ * library). For callers that may not allocate GPU memory while they run a layer, such as
+ * plugin hosts that give a plugin device buffers from their own pool and forbid cudaMalloc
+ * inside it. Same arguments and result as ah_conv3x3_create + ah_conv3x3_run + status,
+ * on the tensor-core kernel only (C % 16 == 0, C <= 128, M <= 256; anything else is rejected
+ * with return 1 and a message). Calls no cudaMalloc / cudaFree: the packed weights, bias
+ * and error word live in a fixed 591,104-byte __device__ array that every GPU that loads the
+ * library keeps until exit. All calls share that array, so calls are serialised on the host
+ * and each returns after its kernel has finished (work overlapping on the GPU would race
+ * on the array). The first call on a device looks up the array's address: make it before
+ * any stream capture on that device. Returns 0, 1 (bad arguments / unsupported) or 2
+ * (CUDA error or a timed-out pipeline wait). */
+int ah_conv3x3_run_noalloc(int device, int C, int M, const uint16_t* w_oihw_f16, const float* bias, int act,
+                           const void* in_nhwc, int H, int W, const void* add1, const void* add2,
+                           void* out_nhwc, void* stream, char* err, int errlen);
+
 /* ------------------------------------------------------------------------------
  * Host fp16 conversions used at load time (no GPU).
  * RNE: hip_engine.cc:1190-1232 (FloatToHalfBitsRNE). FTZ: convert_float_to_float16.cpp:165-186.
