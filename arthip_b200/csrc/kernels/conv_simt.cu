@@ -152,6 +152,91 @@ __global__ void __launch_bounds__(kSimtThreads) conv3x3_simt_kernel(const SimtAr
   }
 }
 
+// Single-input-channel head conv (C == 1, M % 8 == 0, plain NHWC fp16 output): each thread
+// owns 8 output channels, keeps their 72 weights and 8 biases in registers, and walks
+// kC1Run consecutive pixels of one row with a sliding 3x3 input window (3 new loads per
+// pixel). Same accumulation order and epilogue as conv3x3_simt_kernel (tap-major fp32
+// FMAs from zero, then + bias and the fp16 node rounding), so both give identical bits.
+constexpr int kC1Run = 16;
+
+__global__ void __launch_bounds__(kSimtThreads) conv3x3_c1_kernel(const SimtArgs a) {
+  const int G = a.groups;  // M / 8
+  const int t = blockIdx.x * blockDim.x + threadIdx.x;
+  const int runs = (a.W + kC1Run - 1) / kC1Run;
+  if (t >= runs * G) return;
+  const int g = t % G;
+  const int x0 = (t / G) * kC1Run;
+  const int y = blockIdx.y;
+  const int m0 = g * 8;
+  float w[9][8], b[8];
+#pragma unroll
+  for (int tap = 0; tap < 9; ++tap)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) w[tap][j] = __ldg(a.w + tap * a.M + m0 + j);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) b[j] = __ldg(a.bias + m0 + j);
+  const __half* row[3];
+  bool rv[3];
+#pragma unroll
+  for (int r = 0; r < 3; ++r) {
+    const int yy = y + r - 1;
+    rv[r] = yy >= 0 && yy < a.H;
+    row[r] = a.in + static_cast<long long>(rv[r] ? yy : 0) * a.W;
+  }
+  auto ld = [&](int r, int xx) -> float {
+    return (rv[r] && xx >= 0 && xx < a.W) ? __half2float(__ldg(row[r] + xx)) : 0.f;
+  };
+  float v[3][3];
+#pragma unroll
+  for (int r = 0; r < 3; ++r) {
+    v[r][0] = ld(r, x0 - 1);
+    v[r][1] = ld(r, x0);
+    v[r][2] = ld(r, x0 + 1);
+  }
+  const int xe = min(a.W, x0 + kC1Run);
+  for (int x = x0; x < xe; ++x) {
+    float acc[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+#pragma unroll
+    for (int r = 0; r < 3; ++r)
+#pragma unroll
+      for (int k = 0; k < 3; ++k)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[j] = fmaf(v[r][k], w[r * 3 + k][j], acc[j]);
+    const long long obase = (static_cast<long long>(y) * a.W + x) * a.M + m0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      float t = r16(acc[j] + b[j]);
+      if (a.act == kActRelu) t = fmaxf(t, 0.f);
+      else if (a.act == kActSilu) t = r16(t * r16(1.f / (1.f + expf(-t))));
+      acc[j] = t;
+    }
+    const __half* adds[2] = {a.add1, a.add2};
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      if (!adds[k]) continue;
+      const uint4 u = __ldg(reinterpret_cast<const uint4*>(adds[k] + obase));
+      const __half* q = reinterpret_cast<const __half*>(&u);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[j] = r16(acc[j] + __half2float(q[j]));
+    }
+    uint32_t h[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      __half2 o = __floats2half2_rn(acc[2 * i], acc[2 * i + 1]);
+      h[i] = *reinterpret_cast<uint32_t*>(&o);
+    }
+    *reinterpret_cast<uint4*>(static_cast<__half*>(a.out.ptr) + obase) = make_uint4(h[0], h[1], h[2], h[3]);
+#pragma unroll
+    for (int r = 0; r < 3; ++r) {
+      v[r][0] = v[r][1];
+      v[r][1] = v[r][2];
+      v[r][2] = ld(r, x + 2);
+    }
+  }
+}
+
 template <int MG, bool VEC8>
 cudaError_t launch_simt(const SimtArgs& a, size_t smem, cudaStream_t s) {
   // Weights are staged only when they fit the default 48 KB dynamic shared memory, so no
@@ -210,7 +295,17 @@ cudaError_t simt_conv_launch(const SimtConvWeights& w, const __half* in, int H, 
   const size_t wbytes = static_cast<size_t>(9) * w.C * w.M * sizeof(float);
   a.w_in_smem = wbytes <= static_cast<size_t>(kSimtSmemWeights) ? 1 : 0;
   const size_t smem = a.w_in_smem ? wbytes : 0;
-  const bool vec8 = (w.C % 8 == 0) && ((reinterpret_cast<uintptr_t>(in) & 15u) == 0);
+  auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+  if (w.C == 1 && w.M % 8 == 0 && out.dts_b == 1 && !out.nchw && !out.fp32 && !out.clip && a16(out.ptr) &&
+      a16(add1) && a16(add2)) {
+    a.groups = w.M / 8;
+    const int runs = (W + kC1Run - 1) / kC1Run;
+    const dim3 grid(static_cast<unsigned>((runs * a.groups + kSimtThreads - 1) / kSimtThreads),
+                    static_cast<unsigned>(H));
+    conv3x3_c1_kernel<<<grid, kSimtThreads, 0, s>>>(a);
+    return cudaGetLastError();
+  }
+  const bool vec8 = (w.C % 8 == 0) && a16(in);
   if (w.M <= 4) {
     a.groups = 1;
     return vec8 ? launch_simt<4, true>(a, smem, s) : launch_simt<4, false>(a, smem, s);

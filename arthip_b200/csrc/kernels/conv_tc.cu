@@ -100,6 +100,18 @@ struct SegIter {
 
 __device__ __forceinline__ float r16(float v) { return __half2float(__float2half_rn(v)); }
 
+// Position in a ring of S slots with its phase bit, advanced one step at a time (no integer
+// division in the pipeline loops).
+struct RingPos {
+  uint32_t slot = 0, phase = 0;
+  __device__ __forceinline__ void step(uint32_t S) {
+    if (++slot == S) {
+      slot = 0;
+      phase ^= 1u;
+    }
+  }
+};
+
 // Byte offset of 16-byte granule j of row r in a swizzled K-major tile with `rb`-byte rows
 // (128B / 64B / 32B swizzle: the granule index is XORed with address bits 7.. of the row,
 // for a tile that starts on a 1024-byte boundary).
@@ -141,6 +153,15 @@ __device__ __forceinline__ void epilogue8(uint32_t (&h)[4], int act, const __hal
   if (a2) hadd8(h, a2);
 }
 
+__device__ __forceinline__ void hadd8v(uint32_t (&h)[4], const uint4& u) {
+  const uint32_t* q = reinterpret_cast<const uint32_t*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    __half2 v = __hadd2(*reinterpret_cast<__half2*>(&h[i]), *reinterpret_cast<const __half2*>(&q[i]));
+    h[i] = *reinterpret_cast<uint32_t*>(&v);
+  }
+}
+
 // Compile-time geometry of the input-channel chunks (64-channel chunks first, then at most
 // one 32 and one 16, matching make_chunks on the host). The MMA issue loop is fully
 // unrolled over it, so every descriptor is a register plus a constant: a single issuing
@@ -157,6 +178,29 @@ struct ChunkCfg {
   __host__ __device__ static constexpr int off(int k) { return k == 0 ? 0 : off(k - 1) + area(k - 1); }
   __host__ __device__ static constexpr uint32_t hi(int k) { return ptx::desc_hi(8u * rb(k), layout(k)); }
 };
+
+// The MMAs of one input row in the vertical-window formulation: for every (chunk, kx,
+// k-block) one MMA of N = n1 * M into the window's first TMEM run and, where the window
+// wraps around the accumulator ring (SPLIT), a second one into the run at column 0.
+template <class Cfg, bool SPLIT>
+__device__ __forceinline__ void vert_row_mmas(uint32_t sl, const uint32_t (&bv)[3][Cfg::N], uint32_t M,
+                                              uint32_t ky_lo, uint32_t n1, uint32_t d1, uint32_t d2, uint32_t i1,
+                                              uint32_t i2) {
+#pragma unroll
+  for (int k = 0; k < Cfg::N; ++k) {
+    const uint32_t mrows16 = (M * Cfg::rb(k)) >> 4;  // M weight rows, in 16-byte units
+    const uint32_t b1 = ky_lo * mrows16, b2 = (ky_lo + n1) * mrows16;
+#pragma unroll
+    for (int kx = 0; kx < 3; ++kx)
+#pragma unroll
+      for (int kb = 0; kb < Cfg::kblocks(k); ++kb) {
+        const uint32_t alo = sl + ((Cfg::off(k) + kx * Cfg::rb(k) + kb * 32) >> 4);
+        const uint32_t blo = bv[kx][k] + kb * 2;
+        ptx::mma_f16_ss_acc(d1, alo, Cfg::hi(k), blo + b1, Cfg::hi(k), i1);
+        if (SPLIT) ptx::mma_f16_ss_acc(d2, alo, Cfg::hi(k), blo + b2, Cfg::hi(k), i2);
+      }
+  }
+}
 
 template <int NC64, int NC32, int NC16>
 __global__ void __launch_bounds__(kThreads, 1) conv3x3_tc_kernel(const __grid_constant__ ConvTcArgs a) {
@@ -182,7 +226,8 @@ __global__ void __launch_bounds__(kThreads, 1) conv3x3_tc_kernel(const __grid_co
   const int lane = threadIdx.x & 31;
   const int m0 = blockIdx.y * a.MT;
   const int S = a.nslots;
-  const int NACC = a.nacc;
+  const int NACC = a.nacc;                                      // a power of two
+  const uint32_t lgA = 31 - __clz(static_cast<uint32_t>(NACC));
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
@@ -243,14 +288,15 @@ __global__ void __launch_bounds__(kThreads, 1) conv3x3_tc_kernel(const __grid_co
         ptx::bulk_load(ptx::smem_u32(sW + a.wofs[idx]), src, wrows * a.rowbytes[k], ptx::smem_u32(wbar));
       }
       uint32_t g = 0;
+      RingPos rp;
       SegIter it{t0, t1, a.H};
       Segment sg;
       bool ok = true;
       while (ok && it.next(sg)) {
         const int x0 = sg.strip * kTcTilePx - 1;
-        for (int r = sg.ya - 1; r <= sg.yb; ++r, ++g) {
-          const uint32_t slot = g % S;
-          if (!ptx::mbar_wait(ptx::smem_u32(&empty[slot]), ((g / S) & 1u) ^ 1u, abort_flag)) {
+        for (int r = sg.ya - 1; r <= sg.yb; ++r, ++g, rp.step(S)) {
+          const uint32_t slot = rp.slot;
+          if (!ptx::mbar_wait(ptx::smem_u32(&empty[slot]), rp.phase ^ 1u, abort_flag)) {
             ok = false;
             break;
           }
@@ -286,7 +332,7 @@ __global__ void __launch_bounds__(kThreads, 1) conv3x3_tc_kernel(const __grid_co
       const uint32_t alo0 = ptx::desc_lo(sA_u);
       const uint32_t slot16 = static_cast<uint32_t>(a.slot_bytes) >> 4;
       bool ok = ptx::mbar_wait(ptx::smem_u32(wbar), 0, abort_flag);
-      uint32_t g_base = 0, acc_cnt = 0;
+      uint32_t acc_cnt = 0;
       SegIter it{t0, t1, a.H};
       Segment sg;
       if (a.vert) {
@@ -302,16 +348,18 @@ __global__ void __launch_bounds__(kThreads, 1) conv3x3_tc_kernel(const __grid_co
         for (int kx = 0; kx < 3; ++kx)
 #pragma unroll
           for (int k = 0; k < Cfg::N; ++k) bv[kx][k] = ptx::desc_lo(sW_u + a.wofs[kx * Cfg::N + k]);
-        uint32_t g = 0, obase = 0;
+        const uint32_t lgN = 31 - __clz(NCH);  // NCH is a power of two
+        uint32_t obase = 0;
+        RingPos fp;
         while (ok && it.next(sg)) {
           const int n = sg.yb - sg.ya;
-          for (int j = 0; j <= n + 1 && ok; ++j, ++g) {
-            const uint32_t slot = g % S;
-            ok = ptx::mbar_wait(ptx::smem_u32(&full[slot]), (g / S) & 1u, abort_flag);
+          for (int j = 0; j <= n + 1 && ok; ++j, fp.step(S)) {
+            const uint32_t slot = fp.slot;
+            ok = ptx::mbar_wait(ptx::smem_u32(&full[slot]), fp.phase, abort_flag);
             const int ky_lo = max(0, j - (n - 1)), ky_hi = min(2, j);
             if (ok && ky_lo == 0) {  // output row j starts here: bias-initialise its chunk
               const uint32_t o = obase + j, c = (NCH - (o & (NCH - 1))) & (NCH - 1);
-              ok = ptx::mbar_wait(ptx::smem_u32(&acce[c]), ((o / NCH) & 1u) ^ 1u, abort_flag);
+              ok = ptx::mbar_wait(ptx::smem_u32(&acce[c]), ((o >> lgN) & 1u) ^ 1u, abort_flag);
               ptx::tc_fence_after();
               if (ok) ptx::mma_f16_ss(tmem_base + c * M, ones_desc, biasb_desc, idM, 0);
             }
@@ -323,20 +371,10 @@ __global__ void __launch_bounds__(kThreads, 1) conv3x3_tc_kernel(const __grid_co
             const uint32_t d1 = tmem_base + chi * M, d2 = tmem_base;
             const uint32_t i1 = ptx::idesc_f16_f32(kTcTilePx, n1 * M), i2 = ptx::idesc_f16_f32(kTcTilePx, n2 * M);
             const uint32_t sl = alo0 + slot * slot16;
-#pragma unroll
-            for (int k = 0; k < Cfg::N; ++k) {
-              const uint32_t mrows16 = (M * Cfg::rb(k)) >> 4;  // M weight rows, in 16-byte units
-              const uint32_t b1 = ky_lo * mrows16, b2 = (ky_lo + n1) * mrows16;
-#pragma unroll
-              for (int kx = 0; kx < 3; ++kx)
-#pragma unroll
-                for (int kb = 0; kb < Cfg::kblocks(k); ++kb) {
-                  const uint32_t alo = sl + ((Cfg::off(k) + kx * Cfg::rb(k) + kb * 32) >> 4);
-                  const uint32_t blo = bv[kx][k] + kb * 2;
-                  ptx::mma_f16_ss_acc(d1, alo, Cfg::hi(k), blo + b1, Cfg::hi(k), i1);
-                  if (n2) ptx::mma_f16_ss_acc(d2, alo, Cfg::hi(k), blo + b2, Cfg::hi(k), i2);
-                }
-            }
+            // One branch per row, none per MMA: a branch in the issue stream costs more than
+            // the MMA it guards.
+            if (n2 == 0) vert_row_mmas<Cfg, false>(sl, bv, M, ky_lo, n1, d1, d2, i1, i2);
+            else vert_row_mmas<Cfg, true>(sl, bv, M, ky_lo, n1, d1, d2, i1, i2);
             ptx::mma_commit(ptx::smem_u32(&empty[slot]));
             if (ky_hi == 2) {  // output row j-2 received its last kernel row
               const uint32_t o = obase + j - 2, c = (NCH - (o & (NCH - 1))) & (NCH - 1);
@@ -346,20 +384,21 @@ __global__ void __launch_bounds__(kThreads, 1) conv3x3_tc_kernel(const __grid_co
           obase += n;
         }
       }
+      RingPos rp;  // ring position of the next input row to wait for
       while (ok && !a.vert && it.next(sg)) {
         const int n = sg.yb - sg.ya;
         uint32_t slot[3];
-        for (int ky = 0; ky < 2 && ok; ++ky) {  // the first two rows of the segment
-          slot[ky] = (g_base + ky) % S;
-          ok = ptx::mbar_wait(ptx::smem_u32(&full[slot[ky]]), ((g_base + ky) / S) & 1u, abort_flag);
+        for (int ky = 0; ky < 2 && ok; ++ky, rp.step(S)) {  // the first two rows of the segment
+          slot[ky] = rp.slot;
+          ok = ptx::mbar_wait(ptx::smem_u32(&full[slot[ky]]), rp.phase, abort_flag);
         }
         for (int i = 0; i < n && ok; ++i) {
           // rows i and i+1 of the segment were waited for already; wait for row i+2
-          const uint32_t gl = g_base + i + 2;
-          slot[2] = gl % S;
-          ok = ptx::mbar_wait(ptx::smem_u32(&full[slot[2]]), (gl / S) & 1u, abort_flag);
-          const uint32_t acc = acc_cnt % NACC;
-          if (ok) ok = ptx::mbar_wait(ptx::smem_u32(&acce[acc]), ((acc_cnt / NACC) & 1u) ^ 1u, abort_flag);
+          slot[2] = rp.slot;
+          ok = ptx::mbar_wait(ptx::smem_u32(&full[slot[2]]), rp.phase, abort_flag);
+          rp.step(S);
+          const uint32_t acc = acc_cnt & (NACC - 1);
+          if (ok) ok = ptx::mbar_wait(ptx::smem_u32(&acce[acc]), ((acc_cnt >> lgA) & 1u) ^ 1u, abort_flag);
           if (!ok) break;
           ptx::tc_fence_after();
           const uint32_t d = tmem_base + acc * a.acc_stride;
@@ -383,9 +422,8 @@ __global__ void __launch_bounds__(kThreads, 1) conv3x3_tc_kernel(const __grid_co
           ++acc_cnt;
         }
         if (!ok) break;
-        ptx::mma_commit(ptx::smem_u32(&empty[(g_base + n) % S]));
-        ptx::mma_commit(ptx::smem_u32(&empty[(g_base + n + 1) % S]));
-        g_base += n + 2;
+        ptx::mma_commit(ptx::smem_u32(&empty[slot[0]]));  // the segment's last two rows
+        ptx::mma_commit(ptx::smem_u32(&empty[slot[1]]));
       }
       // Drain every issued MMA before the tensor memory is released.
       ptx::mma_commit(ptx::smem_u32(donebar));
@@ -413,9 +451,28 @@ __global__ void __launch_bounds__(kThreads, 1) conv3x3_tc_kernel(const __grid_co
       for (int y = sg.ya; y < sg.yb; ++y) {
         // accumulator of this output row: ring position -o mod NACC in the vertical
         // formulation (consecutive rows in descending chunks), o mod NACC otherwise
-        const uint32_t acc = a.vert ? ((NACC - (acc_cnt & (NACC - 1))) & (NACC - 1)) : (acc_cnt % NACC);
+        const uint32_t acc = a.vert ? ((NACC - (acc_cnt & (NACC - 1))) & (NACC - 1)) : (acc_cnt & (NACC - 1));
+        const size_t pix = static_cast<size_t>(y) * a.W + (valid ? x : 0);
+        // Residual operands of this warp's first two channel groups, loaded before the
+        // accumulator wait so their DRAM latency overlaps the row's MMAs.
+        uint4 pre[2][2][4];
+        if (o.mode == 0 && valid) {
+#pragma unroll
+          for (int k = 0; k < 2; ++k) {
+            const int g = half + 2 * k;
+            if (g >= ngroups) break;
+            const int cw = min(32, a.MT - g * 32);
+            const size_t off = pix * a.M + m0 + g * 32;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              if (i * 8 >= cw) break;
+              if (a.add1) pre[0][k][i] = __ldg(reinterpret_cast<const uint4*>(a.add1 + off + i * 8));
+              if (a.add2) pre[1][k][i] = __ldg(reinterpret_cast<const uint4*>(a.add2 + off + i * 8));
+            }
+          }
+        }
         int w_ok = 0;
-        if (lane == 0) w_ok = ptx::mbar_wait(ptx::smem_u32(&accf[acc]), (acc_cnt / NACC) & 1u, abort_flag) ? 1 : 0;
+        if (lane == 0) w_ok = ptx::mbar_wait(ptx::smem_u32(&accf[acc]), (acc_cnt >> lgA) & 1u, abort_flag) ? 1 : 0;
         w_ok = __shfl_sync(0xffffffffu, w_ok, 0);
         if (!w_ok) {
           ok = false;
@@ -426,13 +483,17 @@ __global__ void __launch_bounds__(kThreads, 1) conv3x3_tc_kernel(const __grid_co
           if (lane == 0) ptx::bulk_wait_group_read0();  // the staging tiles are free again
           __syncwarp();
         }
-        const size_t pix = static_cast<size_t>(y) * a.W + (valid ? x : 0);
         if (half >= ngroups) {  // no channel group for this warp (MT <= 32): just release
           ptx::tc_fence_before();
           __syncwarp();
           if (lane == 0) ptx::mbar_arrive(ptx::smem_u32(&acce[acc]));
         }
-        for (int g = half, k = 0; g < ngroups; g += 2, ++k) {
+        // At most 4 groups per warp (MT <= 256); unrolled so the prefetched operands of
+        // groups 0 and 1 stay in registers.
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const int g = half + 2 * k;
+          if (g >= ngroups) break;
           const int cw = min(32, a.MT - g * 32);
           uint32_t rr[32];
           const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * a.acc_stride + g * 32;
@@ -457,9 +518,15 @@ __global__ void __launch_bounds__(kThreads, 1) conv3x3_tc_kernel(const __grid_co
                 __half2 v = __floats2half2_rn(__uint_as_float(rr[j8 + 2 * i]), __uint_as_float(rr[j8 + 2 * i + 1]));
                 h[i] = *reinterpret_cast<uint32_t*>(&v);
               }
-              const __half* a1 = (a.add1 && valid) ? a.add1 + pix * a.M + cbase + j8 : nullptr;
-              const __half* a2 = (a.add2 && valid) ? a.add2 + pix * a.M + cbase + j8 : nullptr;
-              epilogue8(h, a.act, a1, a2);
+              if (k < 2) {
+                epilogue8(h, a.act, nullptr, nullptr);
+                if (a.add1 && valid) hadd8v(h, pre[0][k][j8 >> 3]);
+                if (a.add2 && valid) hadd8v(h, pre[1][k][j8 >> 3]);
+              } else {
+                const __half* a1 = (a.add1 && valid) ? a.add1 + pix * a.M + cbase + j8 : nullptr;
+                const __half* a2 = (a.add2 && valid) ? a.add2 + pix * a.M + cbase + j8 : nullptr;
+                epilogue8(h, a.act, a1, a2);
+              }
               *reinterpret_cast<uint4*>(st + swz_granule(lane, j8 >> 3, rb)) = make_uint4(h[0], h[1], h[2], h[3]);
             }
           } else if (valid) {
@@ -635,11 +702,13 @@ size_t conv_tc_pack_layout(int C, int M, ConvTcWeights* L) {
   L->C = C;
   L->M = M;
   L->Mpad = round_up(M, 16);
-  // The vertical-window formulation needs M = 32 or 64 (3M <= 256 columns per MMA and
-  // 512/M ring chunks) and its weights plus 3 row slots resident in shared memory.
-  L->vert = ((M == 32 || M == 64) && smem_need(L, M, true, 0, 3) <= kSmemLimit) ? 1 : 0;
+  // The vertical-window formulation needs Mpad = 16, 32 or 64 (3 * Mpad <= 256 columns per
+  // MMA and a power-of-two ring of Mpad-column chunks) and its weights plus 3 row slots
+  // resident in shared memory.
+  const int Mp = L->Mpad;
+  L->vert = ((Mp == 16 || Mp == 32 || Mp == 64) && smem_need(L, Mp, true, 0, 3) <= kSmemLimit) ? 1 : 0;
   const int nblk = L->vert ? 3 : 9;
-  const int rows = L->vert ? 3 * M : L->Mpad;
+  const int rows = L->vert ? 3 * Mp : Mp;
   long long off = 0;
   for (int b = 0; b < nblk; ++b)
     for (int k = 0; k < L->nchunks; ++k) {
@@ -652,15 +721,17 @@ size_t conv_tc_pack_layout(int C, int M, ConvTcWeights* L) {
 
 void conv_tc_pack_into(const uint16_t* w_oihw, const ConvTcWeights& L, uint8_t* img) {
   std::memset(img, 0, L.wpack_bytes);
-  const int C = L.C, M = L.M;
+  const int C = L.C, M = L.M, Mp = L.Mpad;
   for (int b = 0; b < (L.vert ? 3 : 9); ++b) {
     for (int k = 0; k < L.nchunks; ++k) {
       const ConvTcChunk& ch = L.chunk[k];
       uint8_t* blk = img + L.gofs[b * L.nchunks + k];
-      // standard: block b = tap, row = m; vertical: block b = kx, row = ky * M + m
-      for (int r = 0; r < (L.vert ? 3 * M : M); ++r) {
-        const int m = L.vert ? r % M : r;
-        const int tap = L.vert ? (r / M) * 3 + b : b;
+      // standard: block b = tap, row = m; vertical: block b = kx, row = ky * Mpad + m
+      // (rows of the padding channels m >= M stay zero)
+      for (int r = 0; r < (L.vert ? 3 * Mp : M); ++r) {
+        const int m = L.vert ? r % Mp : r;
+        if (m >= M) continue;
+        const int tap = L.vert ? (r / Mp) * 3 + b : b;
         for (int kk = 0; kk < ch.cw; ++kk) {
           const int c = ch.c0 + kk;
           const uint16_t v = w_oihw[(static_cast<size_t>(m) * C + c) * 9 + tap];
@@ -724,8 +795,8 @@ bool conv_tc_plan(const ConvTcWeights* w, const __half* in, int H, int W, const 
   if (vert) {
     // Whole output-channel range per CTA; deepest input-row ring that fits.
     for (int s = kMaxSlots; s >= 3 && !chosen; --s)
-      if (smem_need(w, w->M, true, out.mode, s) <= kSmemLimit) {
-        chosen = w->M;
+      if (smem_need(w, w->Mpad, true, out.mode, s) <= kSmemLimit) {
+        chosen = w->Mpad;
         slots = s;
       }
   } else {
@@ -774,10 +845,11 @@ bool conv_tc_plan(const ConvTcWeights* w, const __half* in, int H, int W, const 
   off += kEpiWarps * P->stage_per_warp;
   P->smem_bytes = static_cast<size_t>(off) + kTailBytes + 1024;
   if (vert) {
-    // TMEM as a ring of 512 / M chunks of M columns, one per output row in flight.
+    // TMEM as a ring of chunks of M columns (a power of two, at most kMaxAcc of them),
+    // one per output row in flight.
     P->acc_stride = chosen;
-    P->nacc = 512 / chosen;
-    P->tmem_cols = 512;
+    P->nacc = std::min(512 / chosen, kMaxAcc);
+    P->tmem_cols = P->nacc * chosen;
   } else {
     P->acc_stride = round_up(chosen, 32);
     P->nacc = (4 * P->acc_stride <= 512) ? 4 : 2;

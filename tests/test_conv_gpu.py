@@ -52,6 +52,8 @@ TC_CASES = [
     (64, 4, 21, 70, 0, 0),       # narrow tail (N padded to 16, per-element stores)
     (64, 2, 9, 9, 0, 0),
     (32, 12, 7, 140, 1, 1),
+    (48, 16, 33, 150, 2, 1),     # vertical window with N = 48 (chunks 32+16), SiLU, NHWC stores
+    (64, 8, 40, 260, 0, 2),      # vertical window, padded N, per-element stores with two adds
 ]
 
 
@@ -66,7 +68,9 @@ def test_tensor_core_conv_matches_fp32_reference(C, M, H, W, act, nadds):
 
 
 SIMT_CASES = [
-    (1, 64, 40, 77, 0, 0),    # head conv
+    (1, 64, 40, 77, 0, 0),    # head conv (register-weight sliding-window kernel)
+    (1, 32, 19, 45, 2, 2),    # head kernel with SiLU and two residual adds
+    (1, 64, 3, 2000, 1, 0),   # head kernel, rows longer than one block
     (1, 8, 17, 25, 1, 0),
     (3, 64, 16, 33, 2, 0),    # chroma head
     (4, 4, 33, 17, 0, 1),
