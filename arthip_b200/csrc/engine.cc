@@ -526,6 +526,32 @@ bool Engine::Parse(const onnx::Model& model, std::string& error) {
     --i;
   }
 
+  // Clip fusion into a narrow producing conv without DepthToSpace (the chroma / dehalo
+  // tails): the conv's per-element output path applies the bounds after its fp16 rounding,
+  // activation and residual adds, which is the unfused graph's order.
+  for (size_t i = 0; i < ops_.size(); ++i) {
+    if (ops_[i].type != OpType::Clip) continue;
+    const std::string src = ops_[i].in0;
+    size_t p = ops_.size();
+    for (size_t j = 0; j < i; ++j)
+      if (ops_[j].out == src) p = j;
+    if (p == ops_.size() || ops_[p].type != OpType::Conv || ops_[p].fuse_clip) continue;
+    if (weights_[ops_[p].in1].shape[0] > 16) continue;
+    size_t readers = 0;
+    for (const auto& o : ops_) {
+      readers += (o.in0 == src) + (o.type != OpType::Conv && o.in1 == src);
+      for (const auto& a : o.adds) readers += (a == src);
+    }
+    if (readers != 1 || protected_out.count(src) || src == output_name_) continue;
+    OpSpec& conv = ops_[p];
+    conv.fuse_clip = true;
+    conv.clip_min = ops_[i].clip_min;
+    conv.clip_max = ops_[i].clip_max;
+    conv.out = ops_[i].out;
+    ops_.erase(ops_.begin() + static_cast<std::ptrdiff_t>(i));
+    --i;
+  }
+
   // Operand validation: elementwise ops read activations produced inside this graph,
   // never initializer constants or broadcasts (not implemented by the kernels).
   {

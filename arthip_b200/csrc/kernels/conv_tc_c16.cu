@@ -1,0 +1,11 @@
+// Instantiations of the tcgen05 conv kernel for C = 16 input channels (every formulation
+// and output variant), in a file of their own so the variants compile in parallel.
+#include "conv_tc_kernel.cuh"
+
+namespace ah {
+namespace tck {
+
+KernelFn kernel_c16(bool vert, int variant) { return pick<0, 0, 1>(vert, variant); }
+
+}  // namespace tck
+}  // namespace ah

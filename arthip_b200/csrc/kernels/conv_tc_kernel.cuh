@@ -1,0 +1,662 @@
+// Device side of the tcgen05 implicit-GEMM 3x3 convolution (stride 1, SAME padding).
+//
+// Replaces the reference's gfx1100 Winograd WMMA kernel (src/common/hip_kernels.h:143-396)
+// for every conv whose input channel count fits the tensor-core tiling (C % 16 == 0,
+// C <= 128), and the narrow tail conv with its fused DepthToSpace / Clip / boundary
+// cast (the reference's dts_kernel_2d / dts_kernel_in_f32, hip_kernels.h:553-616).
+//
+// GEMM view: one output row segment of 128 pixels is the MMA M dimension, the output
+// channels (padded to 16) are N, and K = 9 taps x C input channels. fp16 operands from
+// shared memory, fp32 accumulators in tensor memory (TMEM). A bias MMA (a constant ones
+// column times the bias row) initialises each accumulator.
+//
+// Data movement:
+//  * input: one TMA tiled load per (input row, channel chunk) brings 130 pixels
+//    (the 128-pixel tile plus a 1-pixel halo each side; out-of-range pixels and rows are
+//    zero-filled by the TMA unit, which is the conv's zero padding) into a ring of row
+//    slots. Each staged row feeds three output rows (ky = 0,1,2); the three horizontal
+//    taps (kx) read the same slot with the descriptor start moved by one pixel row.
+//  * weights: resident in shared memory for the whole persistent kernel, packed on the
+//    host in the swizzled K-major layout the MMA reads.
+//  * accumulators: a ring of NACC tensor-memory accumulators; the epilogue warps drain
+//    one while the MMA warp fills the next.
+//  * epilogue (8 warps; two per TMEM lane quarter, each taking alternate 32-channel
+//    groups): tcgen05.ld -> fp16 rounding (the conv node output) -> ReLU / SiLU -> up to
+//    two residual adds (fp16 adds, as the ONNX Add nodes) -> output.
+//
+// Two MMA formulations (VERT):
+//  * standard: per output row, 9 taps x C/16 MMAs of 128 x MT x 16;
+//  * vertical window (Mpad = 16, 32, 64): an input row feeds output rows j, j-1, j-2
+//    through kernel rows ky = 0, 1, 2; the weights of a (kx, chunk) block hold the three
+//    kernel rows stacked along N, and the three output rows sit in consecutive chunks of
+//    a TMEM ring, so one MMA of N = 3M per (kx, k-block) does all three.
+// Three output forms (EPI): 0 = NHWC fp16 through a swizzled staging tile and TMA stores;
+// 1 = 2x DepthToSpace (DCR) into NCHW with paired stores (upscaler tails); 2 = general
+// per-element DepthToSpace / clip / fp32 / layout stores.
+//
+// Every variant is a separate instantiation (chunk geometry x VERT x EPI x ACT), so each
+// kernel's code holds only its own path: runtime switches in the per-row loops and their
+// code size cost more than the work they select.
+//
+// Warp roles (320 threads): warp 0 = TMA producer, warp 1 = TMEM allocator + MMA issuer
+// (one thread), warps 2..9 = epilogue. Work: the (strip, row) space is split into
+// contiguous ranges, one per CTA; every pipeline wait is time-bounded.
+#pragma once
+
+#include <cstdint>
+
+#include "kernels.h"
+#include "ptx.cuh"
+
+namespace ah {
+namespace tck {
+
+constexpr int kMaxSlots = 8;
+constexpr int kMaxAcc = 16;         // accumulator ring entries (16 = vertical mode, Mpad <= 32)
+constexpr int kEpiWarps = 8;
+constexpr int kThreads = 64 + 32 * kEpiWarps;
+constexpr int kSmemLimit = 232448;  // 227 KB opt-in dynamic shared memory per block
+constexpr int kStageTile = 2048;    // one 32-pixel x 32-channel fp16 staging tile
+constexpr int kTailBytes = 1024;    // barriers and flags
+constexpr int kVariants = 5;        // EPI 0 x ACT {none, relu, silu}; EPI 1; EPI 2
+
+struct ConvTcArgs {
+  CUtensorMap maps[kTcMaxChunks];
+  CUtensorMap out_map32;
+  CUtensorMap out_map16;
+  const uint8_t* wpack;
+  const float* bias;
+  const __half* add1;
+  const __half* add2;
+  uint32_t* status;
+  ConvTcOut out;
+  long long gofs[9 * kTcMaxChunks];
+  int wofs[9 * kTcMaxChunks];
+  int H, W, M, Mpad, MT;
+  int c0[kTcMaxChunks];
+  int slot_off[kTcMaxChunks];
+  int slot_bytes;
+  int slot_tx;  // bytes one row load delivers (all chunks, full boxes)
+  int nslots;
+  int w_smem_bytes;
+  int ones_off, biasb_off, stage_off, stage_per_warp;
+  long long rows_total;
+  int act;
+  int nacc, acc_stride;
+  uint32_t tmem_cols;
+};
+
+typedef void (*KernelFn)(ConvTcArgs);
+
+// The instantiation for an input channel count (C % 16 == 0, 16 <= C <= 128), a
+// formulation and an output variant (0-2: NHWC with act none/relu/silu, 3: 2x DepthToSpace
+// tail, 4: general per-element output).
+KernelFn kernel_for(int C, bool vert, int variant);
+
+struct Segment {
+  int strip, ya, yb;
+};
+
+// Iterates the CTA's contiguous range of (strip, row) tiles as per-strip segments.
+struct SegIter {
+  long long t, t1;
+  int H;
+  __device__ __forceinline__ bool next(Segment& s) {
+    if (t >= t1) return false;
+    s.strip = static_cast<int>(t / H);
+    s.ya = static_cast<int>(t % H);
+    const long long left = t1 - t;
+    s.yb = static_cast<int>(min(static_cast<long long>(H), s.ya + left));
+    t = static_cast<long long>(s.strip) * H + s.yb;
+    return true;
+  }
+};
+
+__device__ __forceinline__ float r16(float v) { return __half2float(__float2half_rn(v)); }
+
+// Position in a ring of S slots with its phase bit, advanced one step at a time (no integer
+// division in the pipeline loops).
+struct RingPos {
+  uint32_t slot = 0, phase = 0;
+  __device__ __forceinline__ void step(uint32_t S) {
+    if (++slot == S) {
+      slot = 0;
+      phase ^= 1u;
+    }
+  }
+};
+
+// Byte offset of 16-byte granule j of row r in a swizzled K-major tile with `rb`-byte rows
+// (128B / 64B / 32B swizzle: the granule index is XORed with address bits 7.. of the row,
+// for a tile that starts on a 1024-byte boundary).
+__host__ __device__ __forceinline__ uint32_t swz_granule(uint32_t r, uint32_t j, uint32_t rb) {
+  const uint32_t phase = rb == 128 ? (r & 7u) : (rb == 64 ? ((r >> 1) & 3u) : ((r >> 2) & 1u));
+  return r * rb + ((j ^ phase) << 4);
+}
+
+__device__ __forceinline__ void hadd8v(uint32_t (&h)[4], const uint4& u) {
+  const uint32_t* q = reinterpret_cast<const uint32_t*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    __half2 v = __hadd2(*reinterpret_cast<__half2*>(&h[i]), *reinterpret_cast<const __half2*>(&q[i]));
+    h[i] = *reinterpret_cast<uint32_t*>(&v);
+  }
+}
+
+// Activation on 8 channels held as 4 half2 (the fp16-rounded conv output).
+template <int ACT>
+__device__ __forceinline__ void act8(uint32_t (&h)[4]) {
+  if constexpr (ACT == kActSilu) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 t = __half22float2(*reinterpret_cast<__half2*>(&h[i]));
+      const float s0 = r16(1.f / (1.f + expf(-t.x)));
+      const float s1 = r16(1.f / (1.f + expf(-t.y)));
+      __half2 o = __floats2half2_rn(t.x * s0, t.y * s1);
+      h[i] = *reinterpret_cast<uint32_t*>(&o);
+    }
+  } else if constexpr (ACT == kActRelu) {
+    const __half2 z = __float2half2_rn(0.f);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      __half2 v = __hmax2(*reinterpret_cast<__half2*>(&h[i]), z);
+      h[i] = *reinterpret_cast<uint32_t*>(&v);
+    }
+  }
+}
+
+// Activation of one fp16-rounded conv output value (runtime selector).
+__device__ __forceinline__ float act1(float t, int act) {
+  if (act == kActRelu) return fmaxf(t, 0.f);
+  if (act == kActSilu) return r16(t * r16(1.f / (1.f + expf(-t))));
+  return t;
+}
+
+// Narrow tail with a fused 2x DepthToSpace (DCR) into an NCHW output, M = 4 * COUT channels
+// all in this thread's accumulator row: output channel c, sub-row r of pixel x takes conv
+// channels (2r)*COUT + c and (2r+1)*COUT + c, which land side by side in the output row, so
+// each (c, r) is one 4-byte (fp16) or 8-byte (fp32) store and a warp writes 128 / 256
+// contiguous bytes per store instruction.
+template <int COUT>
+__device__ __forceinline__ void store_dts2_nchw(const uint32_t (&rr)[32], int act, const ConvTcOut& o, int y, int x,
+                                                int H, int W) {
+  const long long Wo = 2LL * W, plane = 4LL * H * W;
+  const long long row0 = 2LL * y * Wo + 2LL * x;
+#pragma unroll
+  for (int c = 0; c < COUT; ++c)
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      float t[2];
+#pragma unroll
+      for (int q = 0; q < 2; ++q) {
+        float v = act1(r16(__uint_as_float(rr[(2 * r + q) * COUT + c])), act);
+        if (o.clip) v = fminf(fmaxf(v, o.clip_lo), o.clip_hi);
+        t[q] = v;
+      }
+      const long long idx = c * plane + row0 + r * Wo;
+      if (o.fp32) *reinterpret_cast<float2*>(static_cast<float*>(o.ptr) + idx) = make_float2(t[0], t[1]);
+      else *reinterpret_cast<__half2*>(static_cast<__half*>(o.ptr) + idx) = __floats2half2_rn(t[0], t[1]);
+    }
+}
+
+// Compile-time geometry of the input-channel chunks (64-channel chunks first, then at most
+// one 32 and one 16, matching the host's chunking). The MMA issue loop is fully unrolled
+// over it, so every descriptor is a register plus a constant: a single issuing thread
+// keeps the tensor core fed (runtime-computed descriptors cost 77-120 cycles per MMA on
+// B200, above the 48-cycle execution time of a 128x64x16 MMA).
+template <int NC64, int NC32, int NC16>
+struct ChunkCfg {
+  static constexpr int N = NC64 + NC32 + NC16;
+  static constexpr int C = 64 * NC64 + 32 * NC32 + 16 * NC16;
+  __host__ __device__ static constexpr int rb(int k) { return k < NC64 ? 128 : (k < NC64 + NC32 ? 64 : 32); }
+  __host__ __device__ static constexpr int kblocks(int k) { return rb(k) / 32; }
+  __host__ __device__ static constexpr uint32_t layout(int k) { return rb(k) == 128 ? 2u : (rb(k) == 64 ? 4u : 6u); }
+  __host__ __device__ static constexpr int area(int k) { return (136 * rb(k) + 1023) / 1024 * 1024; }
+  __host__ __device__ static constexpr int off(int k) { return k == 0 ? 0 : off(k - 1) + area(k - 1); }
+  __host__ __device__ static constexpr uint32_t hi(int k) { return ptx::desc_hi(8u * rb(k), layout(k)); }
+};
+
+// The MMAs of one input row in the vertical-window formulation: for every (chunk, kx,
+// k-block) one MMA of N = n1 * M into the window's first TMEM run and, where the window
+// wraps around the accumulator ring (SPLIT), a second one into the run at column 0.
+template <class Cfg, bool SPLIT>
+__device__ __forceinline__ void vert_row_mmas(uint32_t sl, const uint32_t (&bv)[3][Cfg::N], uint32_t M,
+                                              uint32_t ky_lo, uint32_t n1, uint32_t d1, uint32_t d2, uint32_t i1,
+                                              uint32_t i2) {
+#pragma unroll
+  for (int k = 0; k < Cfg::N; ++k) {
+    const uint32_t mrows16 = (M * Cfg::rb(k)) >> 4;  // M weight rows, in 16-byte units
+    const uint32_t b1 = ky_lo * mrows16, b2 = (ky_lo + n1) * mrows16;
+#pragma unroll
+    for (int kx = 0; kx < 3; ++kx)
+#pragma unroll
+      for (int kb = 0; kb < Cfg::kblocks(k); ++kb) {
+        const uint32_t alo = sl + ((Cfg::off(k) + kx * Cfg::rb(k) + kb * 32) >> 4);
+        const uint32_t blo = bv[kx][k] + kb * 2;
+        ptx::mma_f16_ss_acc(d1, alo, Cfg::hi(k), blo + b1, Cfg::hi(k), i1);
+        if (SPLIT) ptx::mma_f16_ss_acc(d2, alo, Cfg::hi(k), blo + b2, Cfg::hi(k), i2);
+      }
+  }
+}
+
+template <int NC64, int NC32, int NC16, bool VERT, int EPI, int ACT>
+__global__ void __launch_bounds__(kThreads, 1) conv3x3_tc_kernel(const __grid_constant__ ConvTcArgs a) {
+  using Cfg = ChunkCfg<NC64, NC32, NC16>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sW = smem;
+  uint8_t* sA = smem + a.w_smem_bytes;
+  uint8_t* sOnes = smem + a.ones_off;
+  uint8_t* sBiasB = smem + a.biasb_off;
+  uint8_t* sStage = smem + a.stage_off;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sStage + kEpiWarps * a.stage_per_warp);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + kMaxSlots;
+  uint64_t* accf = bars + 2 * kMaxSlots;
+  uint64_t* acce = accf + kMaxAcc;
+  uint64_t* wbar = acce + kMaxAcc;
+  uint64_t* donebar = wbar + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(donebar + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int m0 = blockIdx.y * a.MT;
+  const int S = a.nslots;
+  const int NACC = a.nacc;  // a power of two
+  const uint32_t lgA = 31 - __clz(static_cast<uint32_t>(NACC));
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      ptx::mbar_init(ptx::smem_u32(&full[s]), 1);
+      ptx::mbar_init(ptx::smem_u32(&empty[s]), 1);
+    }
+    for (int i = 0; i < NACC; ++i) {
+      ptx::mbar_init(ptx::smem_u32(&accf[i]), 1);
+      ptx::mbar_init(ptx::smem_u32(&acce[i]), kEpiWarps);
+    }
+    ptx::mbar_init(ptx::smem_u32(wbar), 1);
+    ptx::mbar_init(ptx::smem_u32(donebar), 1);
+    *abort_flag = 0;
+    ptx::fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+#pragma unroll
+    for (int k = 0; k < Cfg::N; ++k) ptx::prefetch_tensormap(&a.maps[k]);
+  }
+  if (warp == 1) {
+    ptx::tmem_alloc(ptx::smem_u32(tmem_slot), a.tmem_cols);
+    ptx::tmem_relinquish();
+  }
+  // Bias operands (32-byte swizzled rows, 16 K elements): a ones column for the 128
+  // pixel rows, and the bias as column 0 of the MT output-channel rows.
+  for (int r = threadIdx.x; r < kTcTilePx; r += blockDim.x) {
+    uint4* row = reinterpret_cast<uint4*>(sOnes + r * 32);
+    row[0] = make_uint4(0, 0, 0, 0);
+    row[1] = make_uint4(0, 0, 0, 0);
+    *reinterpret_cast<__half*>(sOnes + swz_granule(r, 0, 32)) = __float2half(1.f);
+  }
+  for (int r = threadIdx.x; r < a.MT; r += blockDim.x) {
+    uint4* row = reinterpret_cast<uint4*>(sBiasB + r * 32);
+    row[0] = make_uint4(0, 0, 0, 0);
+    row[1] = make_uint4(0, 0, 0, 0);
+    *reinterpret_cast<__half*>(sBiasB + swz_granule(r, 0, 32)) = __float2half(a.bias[m0 + r]);
+  }
+  ptx::fence_proxy_async_smem();  // the tensor core reads the generic writes above
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const long long t0 = static_cast<long long>(blockIdx.x) * a.rows_total / gridDim.x;
+  const long long t1 = static_cast<long long>(blockIdx.x + 1) * a.rows_total / gridDim.x;
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      // weight blocks: 9 taps x chunks of MT rows, or (vertical) 3 kx x chunks of 3M rows
+      constexpr int nblk = (VERT ? 3 : 9) * Cfg::N;
+      const int wrows = VERT ? 3 * a.MT : a.MT;
+      uint32_t wbytes = 0;
+#pragma unroll
+      for (int idx = 0; idx < nblk; ++idx) wbytes += wrows * Cfg::rb(idx % Cfg::N);
+      ptx::mbar_arrive_expect_tx(ptx::smem_u32(wbar), wbytes);
+#pragma unroll
+      for (int idx = 0; idx < nblk; ++idx) {
+        const int k = idx % Cfg::N;
+        const uint8_t* src = a.wpack + a.gofs[idx] + static_cast<long long>(m0) * Cfg::rb(k);
+        ptx::bulk_load(ptx::smem_u32(sW + a.wofs[idx]), src, wrows * Cfg::rb(k), ptx::smem_u32(wbar));
+      }
+      uint32_t g = 0;
+      RingPos rp;
+      SegIter it{t0, t1, a.H};
+      Segment sg;
+      bool ok = true;
+      while (ok && it.next(sg)) {
+        const int x0 = sg.strip * kTcTilePx - 1;
+        for (int r = sg.ya - 1; r <= sg.yb; ++r, ++g, rp.step(S)) {
+          const uint32_t slot = rp.slot;
+          if (!ptx::mbar_wait(ptx::smem_u32(&empty[slot]), rp.phase ^ 1u, abort_flag)) {
+            ok = false;
+            break;
+          }
+          const uint32_t fb = ptx::smem_u32(&full[slot]);
+          ptx::mbar_arrive_expect_tx(fb, a.slot_tx);
+          const uint32_t dst = ptx::smem_u32(sA + slot * a.slot_bytes);
+#pragma unroll
+          for (int k = 0; k < Cfg::N; ++k) ptx::tma_load_3d(dst + Cfg::off(k), &a.maps[k], fb, a.c0[k], x0, r);
+        }
+      }
+      // Never leave a TMA write in flight at exit: wait (time-bounded) for the last loads.
+      volatile int never_abort = 0;
+      const uint32_t first = g > static_cast<uint32_t>(S) ? g - S : 0u;
+      for (uint32_t j = first; j < g; ++j)
+        ptx::mbar_wait(ptx::smem_u32(&full[j % S]), (j / S) & 1u, &never_abort);
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      const uint32_t sA_u = ptx::smem_u32(sA);
+      const uint32_t sW_u = ptx::smem_u32(sW);
+      const uint64_t ones_desc = ptx::smem_desc(ptx::smem_u32(sOnes), 6, 256);
+      const uint64_t biasb_desc = ptx::smem_desc(ptx::smem_u32(sBiasB), 6, 256);
+      const uint32_t alo0 = ptx::desc_lo(sA_u);
+      const uint32_t slot16 = static_cast<uint32_t>(a.slot_bytes) >> 4;
+      bool ok = ptx::mbar_wait(ptx::smem_u32(wbar), 0, abort_flag);
+      SegIter it{t0, t1, a.H};
+      Segment sg;
+      if constexpr (VERT) {
+        // Input row j of a segment feeds output rows j, j-1, j-2 through kernel rows
+        // ky = 0, 1, 2. Output row o lives in TMEM chunk ring(o) of M columns
+        // (ring(o) = -o mod NCH), so those outputs occupy consecutive chunks and the three
+        // kernel rows (stacked along N in the weight block) go out as one MMA of N = 3M
+        // (split in two where the window wraps around the ring).
+        const uint32_t M = a.MT, NCH = a.nacc;
+        const uint32_t idM = ptx::idesc_f16_f32(kTcTilePx, M);
+        // Low descriptor words of the weight block of every (kx, chunk); the A operand of
+        // a slot is its base word plus a compile-time offset (all shared addresses are
+        // below 256 KB, so adding to the 14-bit start field never carries).
+        uint32_t bv[3][Cfg::N];
+#pragma unroll
+        for (int kx = 0; kx < 3; ++kx)
+#pragma unroll
+          for (int k = 0; k < Cfg::N; ++k) bv[kx][k] = ptx::desc_lo(sW_u + a.wofs[kx * Cfg::N + k]);
+        uint32_t obase = 0;
+        RingPos fp;
+        while (ok && it.next(sg)) {
+          const int n = sg.yb - sg.ya;
+          for (int j = 0; j <= n + 1 && ok; ++j, fp.step(S)) {
+            const uint32_t slot = fp.slot;
+            ok = ptx::mbar_wait(ptx::smem_u32(&full[slot]), fp.phase, abort_flag);
+            const int ky_lo = max(0, j - (n - 1)), ky_hi = min(2, j);
+            if (ok && ky_lo == 0) {  // output row j starts here: bias-initialise its chunk
+              const uint32_t o = obase + j, c = (NCH - (o & (NCH - 1))) & (NCH - 1);
+              ok = ptx::mbar_wait(ptx::smem_u32(&acce[c]), ((o >> lgA) & 1u) ^ 1u, abort_flag);
+              ptx::tc_fence_after();
+              if (ok) ptx::mma_f16_ss(tmem_base + c * M, ones_desc, biasb_desc, idM, 0);
+            }
+            if (!ok) break;
+            const uint32_t ohi = obase + j - ky_lo;
+            const uint32_t chi = (NCH - (ohi & (NCH - 1))) & (NCH - 1);
+            const uint32_t span = ky_hi - ky_lo + 1;
+            const uint32_t n1 = min(span, NCH - chi), n2 = span - n1;
+            const uint32_t d1 = tmem_base + chi * M, d2 = tmem_base;
+            const uint32_t i1 = ptx::idesc_f16_f32(kTcTilePx, n1 * M), i2 = ptx::idesc_f16_f32(kTcTilePx, n2 * M);
+            const uint32_t sl = alo0 + slot * slot16;
+            // One branch per row, none per MMA: a branch in the issue stream costs more than
+            // the MMA it guards.
+            if (n2 == 0) vert_row_mmas<Cfg, false>(sl, bv, M, ky_lo, n1, d1, d2, i1, i2);
+            else vert_row_mmas<Cfg, true>(sl, bv, M, ky_lo, n1, d1, d2, i1, i2);
+            ptx::mma_commit(ptx::smem_u32(&empty[slot]));
+            if (ky_hi == 2) {  // output row j-2 received its last kernel row
+              const uint32_t o = obase + j - 2, c = (NCH - (o & (NCH - 1))) & (NCH - 1);
+              ptx::mma_commit(ptx::smem_u32(&accf[c]));
+            }
+          }
+          obase += n;
+        }
+      } else {
+        const uint32_t idesc = ptx::idesc_f16_f32(kTcTilePx, a.MT);
+        uint32_t blo[9][Cfg::N];
+#pragma unroll
+        for (int t = 0; t < 9; ++t)
+#pragma unroll
+          for (int k = 0; k < Cfg::N; ++k) blo[t][k] = ptx::desc_lo(sW_u + a.wofs[t * Cfg::N + k]);
+        uint32_t acc_cnt = 0;
+        RingPos rp;  // ring position of the next input row to wait for
+        while (ok && it.next(sg)) {
+          const int n = sg.yb - sg.ya;
+          uint32_t slot[3];
+          for (int ky = 0; ky < 2 && ok; ++ky, rp.step(S)) {  // the first two rows of the segment
+            slot[ky] = rp.slot;
+            ok = ptx::mbar_wait(ptx::smem_u32(&full[slot[ky]]), rp.phase, abort_flag);
+          }
+          for (int i = 0; i < n && ok; ++i) {
+            // rows i and i+1 of the segment were waited for already; wait for row i+2
+            slot[2] = rp.slot;
+            ok = ptx::mbar_wait(ptx::smem_u32(&full[slot[2]]), rp.phase, abort_flag);
+            rp.step(S);
+            const uint32_t acc = acc_cnt & (NACC - 1);
+            if (ok) ok = ptx::mbar_wait(ptx::smem_u32(&acce[acc]), ((acc_cnt >> lgA) & 1u) ^ 1u, abort_flag);
+            if (!ok) break;
+            ptx::tc_fence_after();
+            const uint32_t d = tmem_base + acc * a.acc_stride;
+            ptx::mma_f16_ss(d, ones_desc, biasb_desc, idesc, 0);  // D = bias
+#pragma unroll
+            for (int ky = 0; ky < 3; ++ky) {
+              const uint32_t sl = alo0 + slot[ky] * slot16;
+#pragma unroll
+              for (int k = 0; k < Cfg::N; ++k)
+#pragma unroll
+                for (int kx = 0; kx < 3; ++kx)
+#pragma unroll
+                  for (int kb = 0; kb < Cfg::kblocks(k); ++kb)
+                    ptx::mma_f16_ss_acc(d, sl + ((Cfg::off(k) + kx * Cfg::rb(k) + kb * 32) >> 4), Cfg::hi(k),
+                                        blo[ky * 3 + kx][k] + kb * 2, Cfg::hi(k), idesc);
+            }
+            ptx::mma_commit(ptx::smem_u32(&accf[acc]));
+            ptx::mma_commit(ptx::smem_u32(&empty[slot[0]]));
+            slot[0] = slot[1];
+            slot[1] = slot[2];
+            ++acc_cnt;
+          }
+          if (!ok) break;
+          ptx::mma_commit(ptx::smem_u32(&empty[slot[0]]));  // the segment's last two rows
+          ptx::mma_commit(ptx::smem_u32(&empty[slot[1]]));
+        }
+      }
+      // Drain every issued MMA before the tensor memory is released.
+      ptx::mma_commit(ptx::smem_u32(donebar));
+      volatile int never_abort = 0;
+      ptx::mbar_wait(ptx::smem_u32(donebar), 0, &never_abort);
+    }
+    __syncwarp();
+  } else {
+    // ---------------- epilogue (warps 2..9) ----------------
+    const int e = warp - 2;
+    const int q = warp & 3;   // tensor-memory lane quarter this warp may access
+    const int half = e >> 2;  // this warp takes channel groups half, half+2, ...
+    const int ngroups = (a.MT + 31) / 32;
+    const int act = ACT >= 0 ? ACT : a.act;
+    uint8_t* stage = sStage + e * a.stage_per_warp;
+    const ConvTcOut& o = a.out;
+    uint32_t acc_cnt = 0;
+    SegIter it{t0, t1, a.H};
+    Segment sg;
+    bool ok = true;
+    bool stores_pending = false;
+    while (ok && it.next(sg)) {
+      const int xw = sg.strip * kTcTilePx + q * 32;  // first pixel of this warp's 32
+      const int x = xw + lane;
+      const bool valid = x < a.W;
+      for (int y = sg.ya; y < sg.yb; ++y) {
+        // accumulator of this output row: ring position -o mod NACC in the vertical
+        // formulation (consecutive rows in descending chunks), o mod NACC otherwise
+        const uint32_t acc = VERT ? ((NACC - (acc_cnt & (NACC - 1))) & (NACC - 1)) : (acc_cnt & (NACC - 1));
+        const size_t pix = static_cast<size_t>(y) * a.W + (valid ? x : 0);
+        // Residual operands of this warp's first two channel groups, loaded before the
+        // accumulator wait so their DRAM latency overlaps the row's MMAs.
+        uint4 pre[2][2][4];
+        if constexpr (EPI == 0) {
+          if (valid && a.add1) {
+#pragma unroll
+            for (int k = 0; k < 2; ++k) {
+              const int g = half + 2 * k;
+              if (g >= ngroups) break;
+              const int cw = min(32, a.MT - g * 32);
+              const size_t off = pix * a.M + m0 + g * 32;
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                if (i * 8 >= cw) break;
+                pre[0][k][i] = __ldg(reinterpret_cast<const uint4*>(a.add1 + off + i * 8));
+                if (a.add2) pre[1][k][i] = __ldg(reinterpret_cast<const uint4*>(a.add2 + off + i * 8));
+              }
+            }
+          }
+        }
+        int w_ok = 0;
+        if (lane == 0) w_ok = ptx::mbar_wait(ptx::smem_u32(&accf[acc]), (acc_cnt >> lgA) & 1u, abort_flag) ? 1 : 0;
+        w_ok = __shfl_sync(0xffffffffu, w_ok, 0);
+        if (!w_ok) {
+          ok = false;
+          break;
+        }
+        ptx::tc_fence_after();
+        if constexpr (EPI == 0) {
+          if (stores_pending) {
+            if (lane == 0) ptx::bulk_wait_group_read0();  // the staging tiles are free again
+            __syncwarp();
+          }
+        }
+        if (half >= ngroups) {  // no channel group for this warp (MT <= 32): just release
+          ptx::tc_fence_before();
+          __syncwarp();
+          if (lane == 0) ptx::mbar_arrive(ptx::smem_u32(&acce[acc]));
+        }
+        // At most 4 groups per warp (MT <= 256); unrolled so the prefetched operands of
+        // groups 0 and 1 stay in registers.
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const int g = half + 2 * k;
+          if (g >= ngroups) break;
+          const int cw = min(32, a.MT - g * 32);
+          uint32_t rr[32];
+          const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * a.acc_stride + g * 32;
+          if (cw == 32) ptx::tmem_ld_32x32b_x32(taddr, rr);
+          else ptx::tmem_ld_32x32b_x16(taddr, rr);
+          ptx::tmem_wait_ld();
+          if (g + 2 >= ngroups) {  // this warp's last group: release the accumulator
+            ptx::tc_fence_before();
+            __syncwarp();
+            if (lane == 0) ptx::mbar_arrive(ptx::smem_u32(&acce[acc]));
+          }
+          const int cbase = m0 + g * 32;
+          if constexpr (EPI == 0) {
+            uint8_t* st = stage + k * kStageTile;
+            const uint32_t rb = cw * 2;
+#pragma unroll
+            for (int j8 = 0; j8 < 32; j8 += 8) {
+              if (j8 >= cw) break;
+              uint32_t h[4];
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                __half2 v = __floats2half2_rn(__uint_as_float(rr[j8 + 2 * i]), __uint_as_float(rr[j8 + 2 * i + 1]));
+                h[i] = *reinterpret_cast<uint32_t*>(&v);
+              }
+              act8<ACT>(h);
+              if (valid && a.add1) {
+                if (k < 2) {
+                  hadd8v(h, pre[0][k][j8 >> 3]);
+                  if (a.add2) hadd8v(h, pre[1][k][j8 >> 3]);
+                } else {
+                  const size_t off = pix * a.M + cbase + j8;
+                  hadd8v(h, __ldg(reinterpret_cast<const uint4*>(a.add1 + off)));
+                  if (a.add2) hadd8v(h, __ldg(reinterpret_cast<const uint4*>(a.add2 + off)));
+                }
+              }
+              *reinterpret_cast<uint4*>(st + swz_granule(lane, j8 >> 3, rb)) = make_uint4(h[0], h[1], h[2], h[3]);
+            }
+          } else if constexpr (EPI == 1) {
+            if (valid) {
+              switch (a.M >> 2) {
+                case 1: store_dts2_nchw<1>(rr, act, o, y, x, a.H, a.W); break;
+                case 2: store_dts2_nchw<2>(rr, act, o, y, x, a.H, a.W); break;
+                case 3: store_dts2_nchw<3>(rr, act, o, y, x, a.H, a.W); break;
+                default: store_dts2_nchw<4>(rr, act, o, y, x, a.H, a.W); break;
+              }
+            }
+          } else {
+            if (valid) {
+              // General narrow outputs: per-element DepthToSpace (DCR) / clip / dtype / layout.
+              const int b = o.dts_b;
+              const int cout = a.M / (b * b);
+              const long long Ho = static_cast<long long>(a.H) * b, Wo = static_cast<long long>(a.W) * b;
+#pragma unroll
+              for (int j = 0; j < 32; ++j) {
+                const int m = cbase + j;
+                if (j >= cw || m >= a.M) break;
+                float t = act1(r16(__uint_as_float(rr[j])), act);
+                if (a.add1) t = r16(t + __half2float(a.add1[pix * a.M + m]));
+                if (a.add2) t = r16(t + __half2float(a.add2[pix * a.M + m]));
+                if (o.clip) t = fminf(fmaxf(t, o.clip_lo), o.clip_hi);
+                const int rq = m / cout, c = m - rq * cout;
+                const int r_ = rq / b, q_ = rq - r_ * b;
+                const long long oy = static_cast<long long>(y) * b + r_, ox = static_cast<long long>(x) * b + q_;
+                const long long idx =
+                    o.nchw ? ((static_cast<long long>(c) * Ho + oy) * Wo + ox) : ((oy * Wo + ox) * cout + c);
+                if (o.fp32) static_cast<float*>(o.ptr)[idx] = t;
+                else static_cast<__half*>(o.ptr)[idx] = __float2half_rn(t);
+              }
+            }
+          }
+        }
+        if constexpr (EPI == 0) {
+          ptx::fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0 && xw < a.W) {
+            for (int g = half, k = 0; g < ngroups; g += 2, ++k) {
+              const int cw = min(32, a.MT - g * 32);
+              const uint32_t src = ptx::smem_u32(stage + k * kStageTile);
+              ptx::tma_store_3d(cw == 32 ? &a.out_map32 : &a.out_map16, src, m0 + g * 32, xw, y);
+            }
+            ptx::bulk_commit_group();
+          }
+          stores_pending = true;
+        }
+        ++acc_cnt;
+      }
+    }
+    if constexpr (EPI == 0) {
+      if (lane == 0) ptx::bulk_wait_group0();
+    }
+    __syncwarp();
+  }
+
+  ptx::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    ptx::tc_fence_after();
+    ptx::tmem_dealloc(tmem_base, a.tmem_cols);
+  }
+  if (threadIdx.x == 0 && *abort_flag) atomicOr(a.status, 1u);
+}
+
+// All output variants of one chunk geometry and formulation.
+template <int NC64, int NC32, int NC16, bool VERT>
+KernelFn pick_variant(int variant) {
+  switch (variant) {
+    case 0: return conv3x3_tc_kernel<NC64, NC32, NC16, VERT, 0, kActNone>;
+    case 1: return conv3x3_tc_kernel<NC64, NC32, NC16, VERT, 0, kActRelu>;
+    case 2: return conv3x3_tc_kernel<NC64, NC32, NC16, VERT, 0, kActSilu>;
+    case 3: return conv3x3_tc_kernel<NC64, NC32, NC16, VERT, 1, -1>;
+    default: return conv3x3_tc_kernel<NC64, NC32, NC16, VERT, 2, -1>;
+  }
+}
+
+template <int NC64, int NC32, int NC16>
+KernelFn pick(bool vert, int variant) {
+  return vert ? pick_variant<NC64, NC32, NC16, true>(variant) : pick_variant<NC64, NC32, NC16, false>(variant);
+}
+
+}  // namespace tck
+}  // namespace ah

@@ -96,6 +96,66 @@ def conv_chain(spec: ChainSpec, seed: int) -> ChainModel:
     return ChainModel(op.Model(graph=g, opset=OPSET), convs, spec)
 
 
+def artcnn_silu(blocks: int = 8, features: int = 64, in_ch: int = 1, out_ch: int = 1, scale: int = 2,
+                fp32_io: bool = False, seed: int = 0) -> ChainModel:
+    """The topology of the shipped ArtCNN models (random weights of the same shapes):
+    ``head conv -> N x [conv+SiLU, conv+SiLU, conv, add block input] -> conv -> add head
+    output -> tail conv -> DepthToSpace(scale, DCR) (scale > 1) -> Clip(0, 1)``, with SiLU
+    as Sigmoid + Mul, ``auto_pad = SAME_UPPER`` convs and Clip bounds as initializers.
+    ``fp32_io`` wraps the fp16 graph in boundary Casts (fp32 input and output), as the
+    fp32 chroma / dehalo models look after fp16 conversion with kept IO types."""
+    rng = np.random.default_rng(seed + 2000)
+    nodes, inits, convs = [], [], []
+    f = features
+
+    def conv(x, m, c, out, wscale=1.0):
+        w = _he(rng, m, c, wscale)
+        bias = (rng.standard_normal(m) * 0.01).astype(np.float16)
+        inits.append(op.tensor_from_array(f"{out}_w", w))
+        inits.append(op.tensor_from_array(f"{out}_b", bias))
+        nodes.append(op.make_node("Conv", [x, f"{out}_w", f"{out}_b"], [out], kernel_shape=[3, 3],
+                                  auto_pad="SAME_UPPER", strides=[1, 1], dilations=[1, 1], group=1))
+        convs.append((w, bias))
+        return out
+
+    def silu(x, out):
+        nodes.append(op.make_node("Sigmoid", [x], [f"{out}_sig"]))
+        nodes.append(op.make_node("Mul", [x, f"{out}_sig"], [out]))
+        return out
+
+    src = "input"
+    if fp32_io:
+        nodes.append(op.make_node("Cast", ["input"], ["input_h"], to=op.FLOAT16))
+        src = "input_h"
+    h = conv(src, f, in_ch, "head")
+    x = h
+    for i in range(blocks):
+        a = silu(conv(x, f, f, f"b{i}_a"), f"b{i}_as")
+        b = silu(conv(a, f, f, f"b{i}_b"), f"b{i}_bs")
+        c = conv(b, f, f, f"b{i}_c", wscale=0.1)
+        nodes.append(op.make_node("Add", [c, x], [f"b{i}_s"]))
+        x = f"b{i}_s"
+    body = conv(x, f, f, "body")
+    nodes.append(op.make_node("Add", [body, h], ["skip"]))
+    t = conv("skip", out_ch * scale * scale, f, "tail")
+    if scale > 1:
+        nodes.append(op.make_node("DepthToSpace", [t], ["dts"], blocksize=scale, mode="DCR"))
+        t = "dts"
+    inits.append(op.tensor_from_array("clip_lo", np.array(0.0, dtype=np.float16)))
+    inits.append(op.tensor_from_array("clip_hi", np.array(1.0, dtype=np.float16)))
+    out = "clipped" if fp32_io else "output"
+    nodes.append(op.make_node("Clip", [t, "clip_lo", "clip_hi"], [out]))
+    if fp32_io:
+        nodes.append(op.make_node("Cast", [out], ["output"], to=op.FLOAT))
+    io = op.FLOAT if fp32_io else op.FLOAT16
+    g = op.Graph(nodes=nodes,
+                 inputs=[op.value_info("input", io, [1, in_ch, "H", "W"])],
+                 outputs=[op.value_info("output", io, [1, out_ch, "H2", "W2"])],
+                 initializers=inits, name=f"artcnn_silu_b{blocks}f{f}")
+    spec = ChainSpec(f"SiLU-B{blocks}F{f}", blocks, f, in_ch, out_ch, scale)
+    return ChainModel(op.Model(graph=g, opset=19), convs, spec)
+
+
 def synthetic_frame(seed: int, c: int, h: int, w: int) -> np.ndarray:
     """Seeded U[0,1) frame, NCHW float16."""
     rng = np.random.default_rng(seed)

@@ -111,3 +111,23 @@ def test_shipped_chroma_model_folds_fp32_casts(tmp_path):
     info = inspect_model(path)
     assert info["in_fp32"] and info["out_fp32"]
     assert info["in_channels"] == 3 and info["out_channels"] == 2
+    ops = [l for l in info["ops"] if not l.startswith(("input", "output"))]
+    assert len(ops) == 27 and all(l.startswith("Conv") for l in ops)
+    assert "clip[0,1]" in ops[-1]  # Clip fused into the 2-channel tail conv
+
+
+@pytest.mark.parametrize("kw", [dict(in_ch=1, out_ch=1, scale=2), dict(in_ch=3, out_ch=2, scale=1, fp32_io=True),
+                                dict(in_ch=3, out_ch=3, scale=2, fp32_io=True)])
+def test_artcnn_silu_topology_fuses_to_one_op_per_conv(tmp_path, kw):
+    """The shipped ArtCNN topology (SiLU blocks, body conv + global skip, tail, optional
+    DepthToSpace, Clip, optional fp32 boundary Casts) fuses to its 27 convs."""
+    cm = modelgen.artcnn_silu(seed=5, **kw)
+    p = tmp_path / "m.onnx"
+    op.save_model(cm.model, p)
+    info = inspect_model(p)
+    ops = [l for l in info["ops"] if not l.startswith(("input", "output"))]
+    assert len(ops) == 27 and all(l.startswith("Conv") for l in ops)
+    assert sum("+silu" in l for l in ops) == 16
+    assert sum("+add" in l for l in ops) == 9
+    assert "clip[0,1]" in ops[-1] and (("+dts2" in ops[-1]) == (kw["scale"] == 2))
+    assert info["in_fp32"] == info["out_fp32"] == kw.get("fp32_io", False)
