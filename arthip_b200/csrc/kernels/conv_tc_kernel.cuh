@@ -494,6 +494,15 @@ __global__ void __launch_bounds__(kThreads, 1) conv3x3_tc_kernel(const __grid_co
         // formulation (consecutive rows in descending chunks), o mod NACC otherwise
         const uint32_t acc = VERT ? ((NACC - (acc_cnt & (NACC - 1))) & (NACC - 1)) : (acc_cnt & (NACC - 1));
         const size_t pix = static_cast<size_t>(y) * a.W + (valid ? x : 0);
+        if constexpr (EPI == 0) {
+          // Residual lines of the row two ahead go to L2 now, so the register loads below
+          // (issued one accumulator wait ahead) hit L2 instead of DRAM.
+          if (valid && a.add1 && half < ngroups && y + 2 < sg.yb) {
+            const size_t off = (pix + 2 * static_cast<size_t>(a.W)) * a.M + m0 + half * 32;
+            ptx::prefetch_l2(a.add1 + off);
+            if (a.add2) ptx::prefetch_l2(a.add2 + off);
+          }
+        }
         // Residual operands of this warp's first two channel groups, loaded before the
         // accumulator wait so their DRAM latency overlaps the row's MMAs.
         uint4 pre[2][2][4];
