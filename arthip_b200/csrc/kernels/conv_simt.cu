@@ -268,14 +268,21 @@ cudaError_t simt_conv_upload(const uint16_t* w_oihw, const float* bias, int C, i
   if (e != cudaSuccess) return e;
   e = cudaMalloc(&out->bias, sizeof(float) * M);
   if (e != cudaSuccess) return e;
-  return cudaMemcpy(out->bias, b.data(), sizeof(float) * M, cudaMemcpyHostToDevice);
+  e = cudaMemcpy(out->bias, b.data(), sizeof(float) * M, cudaMemcpyHostToDevice);
+  if (e != cudaSuccess || !head_mma_supported(C, M)) return e;
+  const std::vector<uint32_t> f = head_mma_fragments(w_oihw, C, M);
+  e = cudaMalloc(&out->bfrag, f.size() * sizeof(uint32_t));
+  if (e != cudaSuccess) return e;
+  return cudaMemcpy(out->bfrag, f.data(), f.size() * sizeof(uint32_t), cudaMemcpyHostToDevice);
 }
 
 void simt_conv_free(SimtConvWeights* w) {
   if (w->w) cudaFree(w->w);
   if (w->bias) cudaFree(w->bias);
+  if (w->bfrag) cudaFree(w->bfrag);
   w->w = nullptr;
   w->bias = nullptr;
+  w->bfrag = nullptr;
 }
 
 cudaError_t simt_conv_launch(const SimtConvWeights& w, const __half* in, int H, int W, const __half* add1,
@@ -296,6 +303,9 @@ cudaError_t simt_conv_launch(const SimtConvWeights& w, const __half* in, int H, 
   a.w_in_smem = wbytes <= static_cast<size_t>(kSimtSmemWeights) ? 1 : 0;
   const size_t smem = a.w_in_smem ? wbytes : 0;
   auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+  const bool plain = out.dts_b == 1 && !out.nchw && !out.fp32 && !out.clip;
+  if (w.bfrag && plain && !add1 && !add2 && a16(out.ptr))
+    return head_mma_launch(w.bfrag, w.bias, w.C, w.M, in, H, W, act, static_cast<__half*>(out.ptr), s);
   if (w.C == 1 && w.M % 8 == 0 && out.dts_b == 1 && !out.nchw && !out.fp32 && !out.clip && a16(out.ptr) &&
       a16(add1) && a16(add2)) {
     a.groups = w.M / 8;

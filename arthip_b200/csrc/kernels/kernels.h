@@ -118,12 +118,21 @@ struct SimtConvWeights {
   int C = 0, M = 0;
   float* w = nullptr;    // device: [tap][c][m] fp32 (values of the fp16 weights)
   float* bias = nullptr; // device: M fp32
+  uint32_t* bfrag = nullptr;  // device: mma.sync B fragments of the tensor-core head (conv_head.cu)
 };
 cudaError_t simt_conv_upload(const uint16_t* w_oihw_f16, const float* bias_or_null, int C, int M,
                              SimtConvWeights* out);
 void simt_conv_free(SimtConvWeights* w);
 cudaError_t simt_conv_launch(const SimtConvWeights& w, const __half* in, int H, int W, const __half* add1,
                              const __half* add2, int act, const SimtOut& out, cudaStream_t stream);
+
+// Tensor-core (mma.sync) head conv for C <= 4 input channels, M in {32, 64, 96, 128},
+// plain NHWC fp16 output without residual adds (conv_head.cu). simt_conv_upload /
+// simt_conv_launch use it when it applies.
+bool head_mma_supported(int C, int M);
+std::vector<uint32_t> head_mma_fragments(const uint16_t* w_oihw_f16, int C, int M);
+cudaError_t head_mma_launch(const uint32_t* bfrag, const float* bias, int C, int M, const __half* in, int H, int W,
+                            int act, __half* out, cudaStream_t s);
 
 // ---------------------------------------------------------------------------
 // Pointwise / layout kernels (pointwise.cu)

@@ -15,7 +15,7 @@ import pytest
 
 from arthip_b200 import modelgen, onnx_proto as op
 from arthip_b200.engine import Engine
-from gpu_util import assert_frame_parity
+from gpu_util import assert_frame_parity, check_against_oracles
 from oracle import onnx_cpu
 
 pytestmark = pytest.mark.gpu
@@ -28,26 +28,9 @@ def _model(tmp_path, cfg, seed):
     return cm, p
 
 
-def _check(got, ref, label, tol=None):
-    return assert_frame_parity(got, ref, label, tol)
-
-
 def _oracle_gap(a, b):
-    """[0,1]-output distance between the two oracle precision variants themselves."""
+    """[0,1]-output distance between two oracle runs."""
     return float(np.abs(np.clip(a, 0, 1) - np.clip(b, 0, 1)).max())
-
-
-def _check_both(got, ref16, ref32, label, spread=0.0):
-    """BASELINE's bar against the typed-graph oracle (fp16 at every node, what an fp16
-    ONNX graph specifies), widened only to the oracle's own accumulation-order spread
-    (`spread`: the same graph with a different fp32 summation order) plus one fp16 ulp at
-    1.0 when that spread already exceeds the bar; against the fp32-between-nodes variant,
-    no farther than the two oracles are from each other plus one ulp (the variants alone
-    differ by 4e-3..5e-3 on these random-weight configs)."""
-    tol16 = 4e-3 if spread <= 4e-3 - 2.0 ** -10 else spread + 2.0 ** -10
-    _check(got, ref16, f"{label} vs oracle fp16_nodes (self-spread {spread:.4g})", tol16)
-    gap = _oracle_gap(ref16, ref32)
-    _check(got, ref32, f"{label} vs oracle fp32_nodes (oracle gap {gap:.4g})", max(4e-3, gap + 2.0 ** -10))
 
 
 @pytest.mark.parametrize("cfg,seed,h,w", [("C4F32", 0, 256, 256), ("R8F64", 2, 96, 160), ("R16F96", 3, 64, 136)])
@@ -56,8 +39,12 @@ def test_config_vs_cpu_oracle(tmp_path, cfg, seed, h, w):
     x = modelgen.synthetic_frame(seed, 1, h, w)
     eng = Engine(p)
     got = eng.run(x).astype(np.float64)
-    refs = [onnx_cpu.run_model(cm.model, x.astype(np.float64), mode=m) for m in ("fp16_nodes", "fp32_nodes")]
-    _check_both(got, refs[0], refs[1], f"{cfg} {h}x{w}")
+    xd = x.astype(np.float64)
+    ref16 = onnx_cpu.run_model(cm.model, xd, mode="fp16_nodes")
+    ref32 = onnx_cpu.run_model(cm.model, xd, mode="fp32_nodes")
+    variants = [onnx_cpu.run_model(cm.model, xd, mode="fp16_nodes", reverse_channels=True),
+                onnx_cpu.run_model(cm.model, xd, mode="fp16_nodes", use_torch=False)]
+    check_against_oracles(got, ref16, ref32, variants, f"{cfg} {h}x{w}")
 
 
 @pytest.mark.parametrize("cfg,seed,h,w", [("R8F64", 2, 1080, 1920), ("R16F96", 3, 1080, 1920),
@@ -72,10 +59,7 @@ def test_config_full_size_vs_fp32_reference(tmp_path, cfg, seed, h, w):
             for m in ("fp16_nodes", "fp32_nodes")]
     alt = onnx_cpu.run_model(cm.model, x.astype(np.float64), mode="fp16_nodes", device="cuda:0",
                              reverse_channels=True)
-    spread = _oracle_gap(refs[0], alt)
-    print(f"{cfg} {h}x{w}: reference self-spread {spread:.4g}, engine vs fp16_nodes "
-          f"{_oracle_gap(got, refs[0]):.4g}, vs fp32_nodes {_oracle_gap(got, refs[1]):.4g}")
-    _check_both(got, refs[0], refs[1], f"{cfg} {h}x{w} (GPU fp32 reference)", spread)
+    check_against_oracles(got, refs[0], refs[1], [alt], f"{cfg} {h}x{w} (GPU fp32 reference)")
 
 
 def test_crop_locality(tmp_path):

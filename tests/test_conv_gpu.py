@@ -72,7 +72,10 @@ SIMT_CASES = [
     (1, 32, 19, 45, 2, 2),    # head kernel with SiLU and two residual adds
     (1, 64, 3, 2000, 1, 0),   # head kernel, rows longer than one block
     (1, 8, 17, 25, 1, 0),
-    (3, 64, 16, 33, 2, 0),    # chroma head
+    (3, 64, 16, 33, 2, 0),    # chroma head (tensor-core head kernel, K = 27 -> 2 k-steps)
+    (2, 32, 9, 300, 1, 0),    # tensor-core head, partial last segment
+    (4, 128, 5, 70, 0, 0),    # tensor-core head, 3 k-steps, 16 channel octets
+    (3, 96, 7, 257, 2, 0),    # tensor-core head, 12 channel octets, one pixel past a segment
     (4, 4, 33, 17, 0, 1),
     (24, 8, 9, 30, 0, 0),     # C not a multiple of 16
     (160, 16, 6, 40, 1, 0),   # wider than the tensor-core tiling: CUDA-core path
