@@ -316,8 +316,10 @@ def main():
               file=sys.stderr)
     print(f"sum of ops {sum(op_ms):.4f} ms/frame (events between ops); graph path {frame_ms:.4f} ms/frame",
           file=sys.stderr)
+    # DRAM bytes per tcgen05 conv launch from the committed one-pass ncu capture of this
+    # workload (ncu cannot run inside a timed bench).
     traffic = None
-    tp = ROOT / "profiles" / "conv_tc_traffic.json"
+    tp = ROOT / "profiles" / "conv3x3_tc_kernel_traffic.json"
     if tp.exists():
         try:
             traffic = json.loads(tp.read_text()).get("dram_bytes_per_launch")
