@@ -113,7 +113,9 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(self.rows), "power_w_max": max(pw) if pw else None}
 
 
-def dist_setup():
+def dist_setup(backend: str = "nccl"):
+    """One process per GPU (torchrun env). The process group carries only the barrier and
+    the max-over-ranks time: frames are independent, so there is no data-path collective."""
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -121,9 +123,12 @@ def dist_setup():
         import datetime
         import torch
         import torch.distributed as dist
-        torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                device_id=torch.device("cuda", local))
+        if backend == "nccl":
+            torch.cuda.set_device(local)
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                    device_id=torch.device("cuda", local))
+        else:
+            dist.init_process_group(backend, timeout=datetime.timedelta(seconds=120))
     return world, rank, local
 
 
@@ -132,9 +137,16 @@ def dist_max(v: float, world: int) -> float:
         return v
     import torch
     import torch.distributed as dist
-    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dev = "cuda" if dist.get_backend() == "nccl" else "cpu"
+    t = torch.tensor([v], dtype=torch.float64, device=dev)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     return float(t.item())
+
+
+def frame_seeds(rank: int, n: int, base: int = SEED) -> list[int]:
+    """Seeds of the synthetic frames rank `rank` processes: each rank works on its own
+    share of the frame stream (weak scaling)."""
+    return [base + 100 * rank + i for i in range(n)]
 
 
 def dist_barrier(world):
@@ -226,8 +238,8 @@ def main():
         ops = eng.ops()
 
         # input ring: 8 distinct synthetic frames resident in HBM
-        ring = torch.stack([torch.from_numpy(modelgen.synthetic_frame(SEED + 100 * rank + i, 1, H, W).reshape(-1))
-                            for i in range(8)]).to(dev)
+        ring = torch.stack([torch.from_numpy(modelgen.synthetic_frame(sd, 1, H, W).reshape(-1))
+                            for sd in frame_seeds(rank, 8)]).to(dev)
         torch.cuda.synchronize()
         estream = torch.cuda.ExternalStream(eng.stream, device=dev)
 
