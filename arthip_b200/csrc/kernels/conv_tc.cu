@@ -6,6 +6,7 @@
 
 #include <algorithm>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <unordered_set>
@@ -346,6 +347,17 @@ cudaError_t conv_tc_launch(const ConvTcPlan& P, const __half* add1, const __half
   a.nacc = P.nacc;
   a.acc_stride = P.acc_stride;
   a.tmem_cols = static_cast<uint32_t>(P.tmem_cols);
+  // Pipeline waits are bounded (4 s). Failure-path test hook, off unless both are set by a
+  // test: ARTHIP_WAIT_LIMIT_MS shortens the bound, ARTHIP_TEST_STALL_ROW makes every CTA
+  // arm that input row's slot without loading it, so the kernel must report a timed-out
+  // wait through the status word (and leave the context usable).
+  a.wait_limit_ns = 4000000000ull;
+  a.stall_row = -1;
+  if (const char* v = std::getenv("ARTHIP_WAIT_LIMIT_MS")) {
+    const long ms = std::strtol(v, nullptr, 10);
+    if (ms > 0 && ms <= 4000) a.wait_limit_ns = static_cast<unsigned long long>(ms) * 1000000ull;
+  }
+  if (const char* v = std::getenv("ARTHIP_TEST_STALL_ROW")) a.stall_row = static_cast<int>(std::strtol(v, nullptr, 10));
   // Output variant: NHWC with a compile-time activation, the 2x DepthToSpace tail (every
   // conv channel in one CTA's first 32-channel group, no residual; NCHW output, which for
   // one output channel is also the NHWC layout), or general stores.

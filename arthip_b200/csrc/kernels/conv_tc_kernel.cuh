@@ -84,6 +84,11 @@ struct ConvTcArgs {
   int act;
   int nacc, acc_stride;
   uint32_t tmem_cols;
+  unsigned long long wait_limit_ns;  // bound of every pipeline wait (4 s)
+  // Failure-path test hook (-1 = off): the producer arms this CTA-relative input row's
+  // slot without loading it, so the MMA issuer's bounded wait for it runs out and the
+  // kernel reports a timed-out wait in the status word instead of hanging.
+  int stall_row;
 };
 
 typedef void (*KernelFn)(ConvTcArgs);
@@ -336,12 +341,13 @@ __global__ void __launch_bounds__(kThreads, 1) conv3x3_tc_kernel(const __grid_co
         const int x0 = sg.strip * kTcTilePx - 1;
         for (int r = sg.ya - 1; r <= sg.yb; ++r, ++g, rp.step(S)) {
           const uint32_t slot = rp.slot;
-          if (!ptx::mbar_wait(ptx::smem_u32(&empty[slot]), rp.phase ^ 1u, abort_flag)) {
+          if (!ptx::mbar_wait(ptx::smem_u32(&empty[slot]), rp.phase ^ 1u, abort_flag, a.wait_limit_ns)) {
             ok = false;
             break;
           }
           const uint32_t fb = ptx::smem_u32(&full[slot]);
           ptx::mbar_arrive_expect_tx(fb, a.slot_tx);
+          if (static_cast<int>(g) == a.stall_row) continue;  // failure-path test: never completes
           const uint32_t dst = ptx::smem_u32(sA + slot * a.slot_bytes);
 #pragma unroll
           for (int k = 0; k < Cfg::N; ++k) ptx::tma_load_3d(dst + Cfg::off(k), &a.maps[k], fb, a.c0[k], x0, r);
@@ -351,7 +357,7 @@ __global__ void __launch_bounds__(kThreads, 1) conv3x3_tc_kernel(const __grid_co
       volatile int never_abort = 0;
       const uint32_t first = g > static_cast<uint32_t>(S) ? g - S : 0u;
       for (uint32_t j = first; j < g; ++j)
-        ptx::mbar_wait(ptx::smem_u32(&full[j % S]), (j / S) & 1u, &never_abort);
+        ptx::mbar_wait(ptx::smem_u32(&full[j % S]), (j / S) & 1u, &never_abort, a.wait_limit_ns);
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
@@ -362,7 +368,7 @@ __global__ void __launch_bounds__(kThreads, 1) conv3x3_tc_kernel(const __grid_co
       const uint64_t biasb_desc = ptx::smem_desc(ptx::smem_u32(sBiasB), 6, 256);
       const uint32_t alo0 = ptx::desc_lo(sA_u);
       const uint32_t slot16 = static_cast<uint32_t>(a.slot_bytes) >> 4;
-      bool ok = ptx::mbar_wait(ptx::smem_u32(wbar), 0, abort_flag);
+      bool ok = ptx::mbar_wait(ptx::smem_u32(wbar), 0, abort_flag, a.wait_limit_ns);
       SegIter it{t0, t1, a.H};
       Segment sg;
       if constexpr (VERT) {
@@ -387,11 +393,11 @@ __global__ void __launch_bounds__(kThreads, 1) conv3x3_tc_kernel(const __grid_co
           const int n = sg.yb - sg.ya;
           for (int j = 0; j <= n + 1 && ok; ++j, fp.step(S)) {
             const uint32_t slot = fp.slot;
-            ok = ptx::mbar_wait(ptx::smem_u32(&full[slot]), fp.phase, abort_flag);
+            ok = ptx::mbar_wait(ptx::smem_u32(&full[slot]), fp.phase, abort_flag, a.wait_limit_ns);
             const int ky_lo = max(0, j - (n - 1)), ky_hi = min(2, j);
             if (ok && ky_lo == 0) {  // output row j starts here: bias-initialise its chunk
               const uint32_t o = obase + j, c = (NCH - (o & (NCH - 1))) & (NCH - 1);
-              ok = ptx::mbar_wait(ptx::smem_u32(&acce[c]), ((o >> lgA) & 1u) ^ 1u, abort_flag);
+              ok = ptx::mbar_wait(ptx::smem_u32(&acce[c]), ((o >> lgA) & 1u) ^ 1u, abort_flag, a.wait_limit_ns);
               ptx::tc_fence_after();
               if (ok) ptx::mma_f16_ss(tmem_base + c * M, ones_desc, biasb_desc, idM, 0);
             }
@@ -429,15 +435,15 @@ __global__ void __launch_bounds__(kThreads, 1) conv3x3_tc_kernel(const __grid_co
           uint32_t slot[3];
           for (int ky = 0; ky < 2 && ok; ++ky, rp.step(S)) {  // the first two rows of the segment
             slot[ky] = rp.slot;
-            ok = ptx::mbar_wait(ptx::smem_u32(&full[slot[ky]]), rp.phase, abort_flag);
+            ok = ptx::mbar_wait(ptx::smem_u32(&full[slot[ky]]), rp.phase, abort_flag, a.wait_limit_ns);
           }
           for (int i = 0; i < n && ok; ++i) {
             // rows i and i+1 of the segment were waited for already; wait for row i+2
             slot[2] = rp.slot;
-            ok = ptx::mbar_wait(ptx::smem_u32(&full[slot[2]]), rp.phase, abort_flag);
+            ok = ptx::mbar_wait(ptx::smem_u32(&full[slot[2]]), rp.phase, abort_flag, a.wait_limit_ns);
             rp.step(S);
             const uint32_t acc = acc_cnt & (NACC - 1);
-            if (ok) ok = ptx::mbar_wait(ptx::smem_u32(&acce[acc]), ((acc_cnt >> lgA) & 1u) ^ 1u, abort_flag);
+            if (ok) ok = ptx::mbar_wait(ptx::smem_u32(&acce[acc]), ((acc_cnt >> lgA) & 1u) ^ 1u, abort_flag, a.wait_limit_ns);
             if (!ok) break;
             ptx::tc_fence_after();
             const uint32_t d = tmem_base + acc * a.acc_stride;
@@ -468,7 +474,7 @@ __global__ void __launch_bounds__(kThreads, 1) conv3x3_tc_kernel(const __grid_co
       // Drain every issued MMA before the tensor memory is released.
       ptx::mma_commit(ptx::smem_u32(donebar));
       volatile int never_abort = 0;
-      ptx::mbar_wait(ptx::smem_u32(donebar), 0, &never_abort);
+      ptx::mbar_wait(ptx::smem_u32(donebar), 0, &never_abort, a.wait_limit_ns);
     }
     __syncwarp();
   } else {
@@ -524,7 +530,7 @@ __global__ void __launch_bounds__(kThreads, 1) conv3x3_tc_kernel(const __grid_co
           }
         }
         int w_ok = 0;
-        if (lane == 0) w_ok = ptx::mbar_wait(ptx::smem_u32(&accf[acc]), (acc_cnt >> lgA) & 1u, abort_flag) ? 1 : 0;
+        if (lane == 0) w_ok = ptx::mbar_wait(ptx::smem_u32(&accf[acc]), (acc_cnt >> lgA) & 1u, abort_flag, a.wait_limit_ns) ? 1 : 0;
         w_ok = __shfl_sync(0xffffffffu, w_ok, 0);
         if (!w_ok) {
           ok = false;

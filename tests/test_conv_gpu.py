@@ -111,3 +111,31 @@ def test_repeated_launches_are_bit_identical():
     torch.cuda.synchronize()
     for o in outs[1:]:
         assert torch.equal(o, outs[0])
+
+
+def test_timed_out_pipeline_wait_is_reported_and_recovers(monkeypatch):
+    """Failure detection without a GPU fault: every CTA arms one input row's slot without
+    loading it, so the MMA issuer's bounded wait (shortened to 50 ms) runs out; the kernel
+    must drain, free its tensor memory and report the timeout in the status word, and the
+    same layer must then run correctly."""
+    from arthip_b200.engine import Conv3x3
+    H, W, C, M = 37, 300, 64, 64
+    g = torch.Generator(device="cpu").manual_seed(5)
+    dev = torch.device("cuda:0")
+    x = torch.rand(1, H, W, C, generator=g).half().to(dev)
+    w = (torch.randn(M, C, 3, 3, generator=g) * (2.0 / (9 * C)) ** 0.5).numpy().astype(np.float16)
+    b = (torch.randn(M, generator=g) * 0.05).numpy().astype(np.float16)
+    out = torch.zeros(1, H, W, M, dtype=torch.float16, device=dev)
+    conv = Conv3x3(w, b.astype(np.float32), act=1)
+    s = torch.cuda.current_stream().cuda_stream
+    monkeypatch.setenv("ARTHIP_WAIT_LIMIT_MS", "50")
+    monkeypatch.setenv("ARTHIP_TEST_STALL_ROW", "1")  # every CTA reads >= 3 input rows
+    conv.run(x.data_ptr(), H, W, out.data_ptr(), stream=s)
+    assert conv.status() != 0, "a wait that cannot complete must be reported"
+    monkeypatch.delenv("ARTHIP_TEST_STALL_ROW")
+    monkeypatch.delenv("ARTHIP_WAIT_LIMIT_MS")
+    conv.run(x.data_ptr(), H, W, out.data_ptr(), stream=s)
+    torch.cuda.synchronize()
+    assert conv.status() == 0
+    ref = torch_conv_layer(x, w, b, 1, [])
+    assert_fp16_layer_close(out.float().cpu().numpy(), ref.cpu().numpy(), "after recovery", ref.abs().cpu().numpy())
