@@ -94,9 +94,10 @@ struct ConvTcArgs {
 typedef void (*KernelFn)(ConvTcArgs);
 
 // The instantiation for an input channel count (C % 16 == 0, 16 <= C <= 128), a
-// formulation and an output variant (0-2: NHWC with act none/relu/silu, 3: 2x DepthToSpace
-// tail, 4: general per-element output).
-KernelFn kernel_for(int C, bool vert, int variant);
+// formulation (vertical window with two pipelines, or one pipeline), and an output variant
+// (0-2: NHWC with act none/relu/silu, 3: 2x DepthToSpace tail, 4: general per-element
+// output; the one-pipeline vertical kernel exists for 0-2 only).
+KernelFn kernel_for(int C, bool vert, int variant, bool dual);
 
 struct Segment {
   int strip, ya, yb;
@@ -656,21 +657,418 @@ __global__ void __launch_bounds__(kThreads, 1) conv3x3_tc_kernel(const __grid_co
   if (threadIdx.x == 0 && *abort_flag) atomicOr(a.status, 1u);
 }
 
-// All output variants of one chunk geometry and formulation.
-template <int NC64, int NC32, int NC16, bool VERT>
-KernelFn pick_variant(int variant) {
-  switch (variant) {
-    case 0: return conv3x3_tc_kernel<NC64, NC32, NC16, VERT, 0, kActNone>;
-    case 1: return conv3x3_tc_kernel<NC64, NC32, NC16, VERT, 0, kActRelu>;
-    case 2: return conv3x3_tc_kernel<NC64, NC32, NC16, VERT, 0, kActSilu>;
-    case 3: return conv3x3_tc_kernel<NC64, NC32, NC16, VERT, 1, -1>;
-    default: return conv3x3_tc_kernel<NC64, NC32, NC16, VERT, 2, -1>;
+// ---------------------------------------------------------------------------
+// Vertical-window formulation with two row pipelines per CTA (384 threads). A single
+// MMA-issuing thread spends ~750 cycles per input row on waits, commits and loop control
+// between its ~1,050 cycles of MMAs, and the tensor core idles meanwhile. Two issuers,
+// each running its own half of the CTA's rows with its own input-slot ring, TMEM ring
+// (half of the 512 columns) and four epilogue warps, keep it busy while sharing one copy
+// of the weights in shared memory.
+//
+// Warps: 0 and 3 = TMA producers (pipe 0 / 1; warp 0 also loads the weights), 1 and 2 =
+// MMA issuers (pipe 0 / 1; warp 1 allocates TMEM), 4..7 = epilogue of pipe 0 and 8..11 =
+// epilogue of pipe 1 (warp w reads TMEM lane quarter w % 4 and all channel groups).
+// ---------------------------------------------------------------------------
+constexpr int kThreads2 = 384;
+
+template <int NC64, int NC32, int NC16, int EPI, int ACT>
+__global__ void __launch_bounds__(kThreads2, 1) conv3x3_tc_vert2_kernel(const __grid_constant__ ConvTcArgs a) {
+  using Cfg = ChunkCfg<NC64, NC32, NC16>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sW = smem;
+  uint8_t* sA = smem + a.w_smem_bytes;  // pipe p, slot s at sA + (p * S + s) * slot_bytes
+  uint8_t* sOnes = smem + a.ones_off;
+  uint8_t* sBiasB = smem + a.biasb_off;
+  uint8_t* sStage = smem + a.stage_off;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sStage + 8 * a.stage_per_warp);
+  uint64_t* full = bars;                       // [2][kMaxSlots]
+  uint64_t* empty = full + 2 * kMaxSlots;      // [2][kMaxSlots]
+  uint64_t* accf = empty + 2 * kMaxSlots;      // [2][kMaxAcc]
+  uint64_t* acce = accf + 2 * kMaxAcc;         // [2][kMaxAcc]
+  uint64_t* wbar = acce + 2 * kMaxAcc;
+  uint64_t* donebar = wbar + 1;                // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(donebar + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int S = a.nslots;           // input-row slots per pipe
+  const int NACC = a.nacc;          // accumulator chunks per pipe (a power of two)
+  const uint32_t lgA = 31 - __clz(static_cast<uint32_t>(NACC));
+  const uint32_t M = a.MT;          // = Mpad: one chunk of M columns per output row
+  const uint32_t half_cols = a.tmem_cols / 2;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 2 * S; ++i) {
+      const int pp = i / S, ss = i - pp * S;
+      ptx::mbar_init(ptx::smem_u32(&full[pp * kMaxSlots + ss]), 1);
+      ptx::mbar_init(ptx::smem_u32(&empty[pp * kMaxSlots + ss]), 1);
+    }
+    for (int i = 0; i < 2 * NACC; ++i) {
+      const int pp = i / NACC, cc = i - pp * NACC;
+      ptx::mbar_init(ptx::smem_u32(&accf[pp * kMaxAcc + cc]), 1);
+      ptx::mbar_init(ptx::smem_u32(&acce[pp * kMaxAcc + cc]), 4);
+    }
+    ptx::mbar_init(ptx::smem_u32(wbar), 1);
+    ptx::mbar_init(ptx::smem_u32(&donebar[0]), 1);
+    ptx::mbar_init(ptx::smem_u32(&donebar[1]), 1);
+    *abort_flag = 0;
+    ptx::fence_mbar_init();
   }
+  if ((warp == 0 || warp == 3) && lane == 0) {
+#pragma unroll
+    for (int k = 0; k < Cfg::N; ++k) ptx::prefetch_tensormap(&a.maps[k]);
+  }
+  if (warp == 1) {
+    ptx::tmem_alloc(ptx::smem_u32(tmem_slot), a.tmem_cols);
+    ptx::tmem_relinquish();
+  }
+  // Bias operands (32-byte swizzled rows, 16 K elements): a ones column for the 128
+  // pixel rows, and the bias as column 0 of the M output-channel rows.
+  for (int r = threadIdx.x; r < kTcTilePx; r += blockDim.x) {
+    uint4* row = reinterpret_cast<uint4*>(sOnes + r * 32);
+    row[0] = make_uint4(0, 0, 0, 0);
+    row[1] = make_uint4(0, 0, 0, 0);
+    *reinterpret_cast<__half*>(sOnes + swz_granule(r, 0, 32)) = __float2half(1.f);
+  }
+  for (int r = threadIdx.x; r < a.MT; r += blockDim.x) {
+    uint4* row = reinterpret_cast<uint4*>(sBiasB + r * 32);
+    row[0] = make_uint4(0, 0, 0, 0);
+    row[1] = make_uint4(0, 0, 0, 0);
+    *reinterpret_cast<__half*>(sBiasB + swz_granule(r, 0, 32)) = __float2half(a.bias[r]);
+  }
+  ptx::fence_proxy_async_smem();  // the tensor core reads the generic writes above
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  // The CTA's contiguous (strip, row) range, split between the two pipes.
+  const long long t0 = static_cast<long long>(blockIdx.x) * a.rows_total / gridDim.x;
+  const long long t1 = static_cast<long long>(blockIdx.x + 1) * a.rows_total / gridDim.x;
+  const long long tm = (t0 + t1) / 2;
+
+  if (warp == 0 || warp == 3) {
+    // ---------------- TMA producers ----------------
+    const int pp = warp == 0 ? 0 : 1;
+    if (lane == 0) {
+      if (pp == 0) {
+        // weight blocks: 3 kx x chunks of 3M rows (the three ky stacked)
+        constexpr int nblk = 3 * Cfg::N;
+        const int wrows = 3 * a.MT;
+        uint32_t wbytes = 0;
+#pragma unroll
+        for (int idx = 0; idx < nblk; ++idx) wbytes += wrows * Cfg::rb(idx % Cfg::N);
+        ptx::mbar_arrive_expect_tx(ptx::smem_u32(wbar), wbytes);
+#pragma unroll
+        for (int idx = 0; idx < nblk; ++idx) {
+          const int k = idx % Cfg::N;
+          ptx::bulk_load(ptx::smem_u32(sW + a.wofs[idx]), a.wpack + a.gofs[idx], wrows * Cfg::rb(k),
+                         ptx::smem_u32(wbar));
+        }
+      }
+      uint64_t* pfull = full + pp * kMaxSlots;
+      uint64_t* pempty = empty + pp * kMaxSlots;
+      uint8_t* pA = sA + static_cast<size_t>(pp) * S * a.slot_bytes;
+      uint32_t g = 0;
+      RingPos rp;
+      SegIter it{pp == 0 ? t0 : tm, pp == 0 ? tm : t1, a.H};
+      Segment sg;
+      bool ok = true;
+      while (ok && it.next(sg)) {
+        const int x0 = sg.strip * kTcTilePx - 1;
+        for (int r = sg.ya - 1; r <= sg.yb; ++r, ++g, rp.step(S)) {
+          const uint32_t slot = rp.slot;
+          if (!ptx::mbar_wait(ptx::smem_u32(&pempty[slot]), rp.phase ^ 1u, abort_flag, a.wait_limit_ns)) {
+            ok = false;
+            break;
+          }
+          const uint32_t fb = ptx::smem_u32(&pfull[slot]);
+          ptx::mbar_arrive_expect_tx(fb, a.slot_tx);
+          if (static_cast<int>(g) == a.stall_row) continue;  // failure-path test: never completes
+          const uint32_t dst = ptx::smem_u32(pA + slot * a.slot_bytes);
+#pragma unroll
+          for (int k = 0; k < Cfg::N; ++k) ptx::tma_load_3d(dst + Cfg::off(k), &a.maps[k], fb, a.c0[k], x0, r);
+        }
+      }
+      // Never leave a TMA write in flight at exit: wait (time-bounded) for the last loads.
+      volatile int never_abort = 0;
+      const uint32_t first = g > static_cast<uint32_t>(S) ? g - S : 0u;
+      for (uint32_t j = first; j < g; ++j)
+        ptx::mbar_wait(ptx::smem_u32(&pfull[j % S]), (j / S) & 1u, &never_abort, a.wait_limit_ns);
+    }
+  } else if (warp == 1 || warp == 2) {
+    // ---------------- MMA issuers ----------------
+    const int pp = warp - 1;
+    if (lane == 0) {
+      uint64_t* pfull = full + pp * kMaxSlots;
+      uint64_t* pempty = empty + pp * kMaxSlots;
+      uint64_t* paccf = accf + pp * kMaxAcc;
+      uint64_t* pacce = acce + pp * kMaxAcc;
+      const uint32_t tbase = tmem_base + pp * half_cols;
+      const uint32_t sA_u = ptx::smem_u32(sA + static_cast<size_t>(pp) * S * a.slot_bytes);
+      const uint32_t sW_u = ptx::smem_u32(sW);
+      const uint64_t ones_desc = ptx::smem_desc(ptx::smem_u32(sOnes), 6, 256);
+      const uint64_t biasb_desc = ptx::smem_desc(ptx::smem_u32(sBiasB), 6, 256);
+      const uint32_t alo0 = ptx::desc_lo(sA_u);
+      const uint32_t slot16 = static_cast<uint32_t>(a.slot_bytes) >> 4;
+      const uint32_t NCH = NACC;
+      const uint32_t idM = ptx::idesc_f16_f32(kTcTilePx, M);
+      // Low descriptor words of the weight block of every (kx, chunk); the A operand of a
+      // slot is its base word plus a compile-time offset (all shared addresses are below
+      // 256 KB, so adding to the 14-bit start field never carries).
+      uint32_t bv[3][Cfg::N];
+#pragma unroll
+      for (int kx = 0; kx < 3; ++kx)
+#pragma unroll
+        for (int k = 0; k < Cfg::N; ++k) bv[kx][k] = ptx::desc_lo(sW_u + a.wofs[kx * Cfg::N + k]);
+      bool ok = ptx::mbar_wait(ptx::smem_u32(wbar), 0, abort_flag, a.wait_limit_ns);
+      SegIter it{pp == 0 ? t0 : tm, pp == 0 ? tm : t1, a.H};
+      Segment sg;
+      uint32_t obase = 0;
+      RingPos fp;
+      // Input row j of a segment feeds output rows j, j-1, j-2 through kernel rows
+      // ky = 0, 1, 2. Output row o lives in chunk ring(o) = -o mod NCH of this pipe's TMEM
+      // half, so those outputs occupy consecutive chunks and one MMA of N = 3M per
+      // (kx, k-block) covers all three (split in two where the window wraps).
+      while (ok && it.next(sg)) {
+        const int n = sg.yb - sg.ya;
+        for (int j = 0; j <= n + 1 && ok; ++j, fp.step(S)) {
+          const uint32_t slot = fp.slot;
+          ok = ptx::mbar_wait(ptx::smem_u32(&pfull[slot]), fp.phase, abort_flag, a.wait_limit_ns);
+          const int ky_lo = max(0, j - (n - 1)), ky_hi = min(2, j);
+          if (ok && ky_lo == 0) {  // output row j starts here: bias-initialise its chunk
+            const uint32_t o = obase + j, c = (NCH - (o & (NCH - 1))) & (NCH - 1);
+            ok = ptx::mbar_wait(ptx::smem_u32(&pacce[c]), ((o >> lgA) & 1u) ^ 1u, abort_flag, a.wait_limit_ns);
+            ptx::tc_fence_after();
+            if (ok) ptx::mma_f16_ss(tbase + c * M, ones_desc, biasb_desc, idM, 0);
+          }
+          if (!ok) break;
+          const uint32_t ohi = obase + j - ky_lo;
+          const uint32_t chi = (NCH - (ohi & (NCH - 1))) & (NCH - 1);
+          const uint32_t span = ky_hi - ky_lo + 1;
+          const uint32_t n1 = min(span, NCH - chi), n2 = span - n1;
+          const uint32_t d1 = tbase + chi * M, d2 = tbase;
+          const uint32_t i1 = ptx::idesc_f16_f32(kTcTilePx, n1 * M), i2 = ptx::idesc_f16_f32(kTcTilePx, n2 * M);
+          const uint32_t sl = alo0 + slot * slot16;
+          // One branch per row, none per MMA.
+          if (n2 == 0) {
+            vert_row_mmas<Cfg, false>(sl, bv, M, ky_lo, n1, d1, d2, i1, i2);
+          } else {
+            vert_row_mmas<Cfg, true>(sl, bv, M, ky_lo, n1, d1, d2, i1, i2);
+          }
+          ptx::mma_commit(ptx::smem_u32(&pempty[slot]));
+          if (ky_hi == 2) {  // output row j-2 received its last kernel row
+            const uint32_t o = obase + j - 2, c = (NCH - (o & (NCH - 1))) & (NCH - 1);
+            ptx::mma_commit(ptx::smem_u32(&paccf[c]));
+          }
+        }
+        obase += n;
+      }
+      // Drain every issued MMA before the tensor memory is released.
+      ptx::mma_commit(ptx::smem_u32(&donebar[pp]));
+      volatile int never_abort = 0;
+      ptx::mbar_wait(ptx::smem_u32(&donebar[pp]), 0, &never_abort, a.wait_limit_ns);
+    }
+    __syncwarp();
+  } else {
+    // ---------------- epilogue (warps 4..11) ----------------
+    const int pp = (warp - 4) >> 2;  // pipe
+    const int q = warp & 3;          // tensor-memory lane quarter this warp may access
+    const int e = warp - 4;
+    const int ngroups = (a.MT + 31) / 32;
+    const int act = ACT >= 0 ? ACT : a.act;
+    uint8_t* stage = sStage + e * a.stage_per_warp;
+    uint64_t* paccf = accf + pp * kMaxAcc;
+    uint64_t* pacce = acce + pp * kMaxAcc;
+    const uint32_t tbase = tmem_base + pp * half_cols;
+    const ConvTcOut& o = a.out;
+    uint32_t acc_cnt = 0;
+    SegIter it{pp == 0 ? t0 : tm, pp == 0 ? tm : t1, a.H};
+    Segment sg;
+    bool ok = true;
+    bool stores_pending = false;
+    while (ok && it.next(sg)) {
+      const int xw = sg.strip * kTcTilePx + q * 32;  // first pixel of this warp's 32
+      const int x = xw + lane;
+      const bool valid = x < a.W;
+      for (int y = sg.ya; y < sg.yb; ++y) {
+        // accumulator of this output row: consecutive rows sit in descending chunks
+        const uint32_t acc = (NACC - (acc_cnt & (NACC - 1))) & (NACC - 1);
+        const size_t pix = static_cast<size_t>(y) * a.W + (valid ? x : 0);
+        uint4 pre[2][2][4];  // [operand][channel group][8 channels]
+        if constexpr (EPI == 0) {
+          if (valid && a.add1) {
+            // Residual lines of the row two ahead go to L2 now; this row's residual
+            // operands are loaded into registers before the accumulator wait.
+            if (y + 2 < sg.yb) {
+#pragma unroll
+              for (int g2 = 0; g2 < 2; ++g2) {
+                if (g2 >= ngroups) break;
+                const size_t off = (pix + 2 * static_cast<size_t>(a.W)) * a.M + g2 * 32;
+                ptx::prefetch_l2(a.add1 + off);
+                if (a.add2) ptx::prefetch_l2(a.add2 + off);
+              }
+            }
+#pragma unroll
+            for (int g2 = 0; g2 < 2; ++g2) {
+              if (g2 >= ngroups) break;
+              const int cw = min(32, a.MT - g2 * 32);
+              const size_t off = pix * a.M + g2 * 32;
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                if (i * 8 >= cw) break;
+                pre[0][g2][i] = __ldg(reinterpret_cast<const uint4*>(a.add1 + off + i * 8));
+                if (a.add2) pre[1][g2][i] = __ldg(reinterpret_cast<const uint4*>(a.add2 + off + i * 8));
+              }
+            }
+          }
+        }
+        int w_ok = 0;
+        if (lane == 0)
+          w_ok = ptx::mbar_wait(ptx::smem_u32(&paccf[acc]), (acc_cnt >> lgA) & 1u, abort_flag, a.wait_limit_ns) ? 1 : 0;
+        w_ok = __shfl_sync(0xffffffffu, w_ok, 0);
+        if (!w_ok) {
+          ok = false;
+          break;
+        }
+        ptx::tc_fence_after();
+        if constexpr (EPI == 0) {
+          if (stores_pending) {
+            if (lane == 0) ptx::bulk_wait_group_read0();  // the staging tiles are free again
+            __syncwarp();
+          }
+        }
+        // Every channel group of this warp's lane quarter (M <= 64: at most 2 groups).
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+          const int g = k;
+          if (g >= ngroups) break;
+          const int cw = min(32, a.MT - g * 32);
+          uint32_t rr[32];
+          const uint32_t taddr = tbase + (static_cast<uint32_t>(q * 32) << 16) + acc * M + g * 32;
+          if (cw == 32) ptx::tmem_ld_32x32b_x32(taddr, rr);
+          else ptx::tmem_ld_32x32b_x16(taddr, rr);
+          ptx::tmem_wait_ld();
+          if (g + 1 >= ngroups) {  // last group read: release the accumulator
+            ptx::tc_fence_before();
+            __syncwarp();
+            if (lane == 0) ptx::mbar_arrive(ptx::smem_u32(&pacce[acc]));
+          }
+          const int cbase = g * 32;
+          if constexpr (EPI == 0) {
+            uint8_t* st = stage + k * kStageTile;
+            const uint32_t rb = cw * 2;
+#pragma unroll
+            for (int j8 = 0; j8 < 32; j8 += 8) {
+              if (j8 >= cw) break;
+              uint32_t h[4];
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                __half2 v = __floats2half2_rn(__uint_as_float(rr[j8 + 2 * i]), __uint_as_float(rr[j8 + 2 * i + 1]));
+                h[i] = *reinterpret_cast<uint32_t*>(&v);
+              }
+              act8<ACT>(h);
+              if (valid && a.add1) {
+                hadd8v(h, pre[0][k][j8 >> 3]);
+                if (a.add2) hadd8v(h, pre[1][k][j8 >> 3]);
+              }
+              *reinterpret_cast<uint4*>(st + swz_granule(lane, j8 >> 3, rb)) = make_uint4(h[0], h[1], h[2], h[3]);
+            }
+          } else if constexpr (EPI == 1) {
+            if (valid) {
+              switch (a.M >> 2) {
+                case 1: store_dts2_nchw<1>(rr, act, o, y, x, a.H, a.W); break;
+                case 2: store_dts2_nchw<2>(rr, act, o, y, x, a.H, a.W); break;
+                case 3: store_dts2_nchw<3>(rr, act, o, y, x, a.H, a.W); break;
+                default: store_dts2_nchw<4>(rr, act, o, y, x, a.H, a.W); break;
+              }
+            }
+          } else {
+            if (valid) {
+              // General narrow outputs: per-element DepthToSpace (DCR) / clip / dtype / layout.
+              const int b = o.dts_b;
+              const int cout = a.M / (b * b);
+              const long long Ho = static_cast<long long>(a.H) * b, Wo = static_cast<long long>(a.W) * b;
+#pragma unroll
+              for (int j = 0; j < 32; ++j) {
+                const int m = cbase + j;
+                if (j >= cw || m >= a.M) break;
+                float t = act1(r16(__uint_as_float(rr[j])), act);
+                if (a.add1) t = r16(t + __half2float(a.add1[pix * a.M + m]));
+                if (a.add2) t = r16(t + __half2float(a.add2[pix * a.M + m]));
+                if (o.clip) t = fminf(fmaxf(t, o.clip_lo), o.clip_hi);
+                const int rq = m / cout, c = m - rq * cout;
+                const int r_ = rq / b, q_ = rq - r_ * b;
+                const long long oy = static_cast<long long>(y) * b + r_, ox = static_cast<long long>(x) * b + q_;
+                const long long idx =
+                    o.nchw ? ((static_cast<long long>(c) * Ho + oy) * Wo + ox) : ((oy * Wo + ox) * cout + c);
+                if (o.fp32) static_cast<float*>(o.ptr)[idx] = t;
+                else static_cast<__half*>(o.ptr)[idx] = __float2half_rn(t);
+              }
+            }
+          }
+        }
+        if constexpr (EPI == 0) {
+          ptx::fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0 && xw < a.W) {
+            for (int g = 0; g < ngroups; ++g) {
+              const int cw = min(32, a.MT - g * 32);
+              const uint32_t src = ptx::smem_u32(stage + g * kStageTile);
+              ptx::tma_store_3d(cw == 32 ? &a.out_map32 : &a.out_map16, src, g * 32, xw, y);
+            }
+            ptx::bulk_commit_group();
+          }
+          stores_pending = true;
+        }
+        ++acc_cnt;
+      }
+    }
+    if constexpr (EPI == 0) {
+      if (lane == 0) ptx::bulk_wait_group0();
+    }
+    __syncwarp();
+  }
+
+  ptx::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    ptx::tc_fence_after();
+    ptx::tmem_dealloc(tmem_base, a.tmem_cols);
+  }
+  if (threadIdx.x == 0 && *abort_flag) atomicOr(a.status, 1u);
 }
 
+// All output variants of one chunk geometry: the standard formulation (conv3x3_tc_kernel),
+// the vertical window with two pipelines (conv3x3_tc_vert2_kernel) and with one
+// (conv3x3_tc_kernel, used for two-residual layers).
 template <int NC64, int NC32, int NC16>
-KernelFn pick(bool vert, int variant) {
-  return vert ? pick_variant<NC64, NC32, NC16, true>(variant) : pick_variant<NC64, NC32, NC16, false>(variant);
+KernelFn pick(bool vert, int variant, bool dual) {
+  if (vert && !dual) {
+    switch (variant) {
+      case 0: return conv3x3_tc_kernel<NC64, NC32, NC16, true, 0, kActNone>;
+      case 1: return conv3x3_tc_kernel<NC64, NC32, NC16, true, 0, kActRelu>;
+      default: return conv3x3_tc_kernel<NC64, NC32, NC16, true, 0, kActSilu>;
+    }
+  }
+  if (vert) {
+    switch (variant) {
+      case 0: return conv3x3_tc_vert2_kernel<NC64, NC32, NC16, 0, kActNone>;
+      case 1: return conv3x3_tc_vert2_kernel<NC64, NC32, NC16, 0, kActRelu>;
+      case 2: return conv3x3_tc_vert2_kernel<NC64, NC32, NC16, 0, kActSilu>;
+      case 3: return conv3x3_tc_vert2_kernel<NC64, NC32, NC16, 1, -1>;
+      default: return conv3x3_tc_vert2_kernel<NC64, NC32, NC16, 2, -1>;
+    }
+  }
+  switch (variant) {
+    case 0: return conv3x3_tc_kernel<NC64, NC32, NC16, false, 0, kActNone>;
+    case 1: return conv3x3_tc_kernel<NC64, NC32, NC16, false, 0, kActRelu>;
+    case 2: return conv3x3_tc_kernel<NC64, NC32, NC16, false, 0, kActSilu>;
+    case 3: return conv3x3_tc_kernel<NC64, NC32, NC16, false, 1, -1>;
+    default: return conv3x3_tc_kernel<NC64, NC32, NC16, false, 2, -1>;
+  }
 }
 
 }  // namespace tck
