@@ -205,6 +205,70 @@ def run_reference(args):
     return 0
 
 
+def run_frame_split(args):
+    """One 7680x4320 frame split into row strips, one per rank, each extended by the
+    model's receptive field (18 rows) so that no halo is exchanged between GPUs. Each rank
+    runs its strip device-resident through the captured CUDA graph; the frame latency is
+    the slowest rank's strip time (CUDA events, max over ranks)."""
+    import tempfile
+
+    import torch
+
+    from arthip_b200 import build as nbuild
+    if not nbuild.LIB_PATH.exists():
+        nbuild.build()
+    from arthip_b200 import modelgen
+    from arthip_b200.engine import Engine
+    from arthip_b200.strips import conv_depth, plan_strips
+
+    H8, W8, seed = 4320, 7680, 4
+    world, rank, local = dist_setup()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    with tempfile.TemporaryDirectory() as td:
+        cm, path = build_model(Path(td))
+        eng = Engine(path, device=local)
+        halo = conv_depth(eng)
+        st = plan_strips(H8, world, halo)[rank]
+        in_ptr, out_ptr, in_bytes, out_bytes = eng.prepare(1, st.rows, W8)
+        frame = modelgen.synthetic_frame(seed, 1, H8, W8)
+        window = torch.from_numpy(np.ascontiguousarray(frame[:, :, st.in_lo:st.in_hi, :]).reshape(-1)).to(dev)
+        estream = torch.cuda.ExternalStream(eng.stream, device=dev)
+
+        class _B:
+            __cuda_array_interface__ = {"shape": (in_bytes // 2,), "typestr": "<f2", "data": (in_ptr, False),
+                                        "version": 3}
+        dst = torch.as_tensor(_B(), device=dev)
+        steps = max(1, min(args.steps, 20))
+        with torch.cuda.stream(estream):
+            dst.copy_(window, non_blocking=True)
+        for _ in range(args.warmup):
+            eng.enqueue()
+        eng.synchronize()
+        dist_barrier(world)
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ev0.record(estream)
+        for _ in range(steps):
+            eng.enqueue()
+        ev1.record(estream)
+        eng.synchronize()
+        torch.cuda.synchronize()
+        ms = dist_max(ev0.elapsed_time(ev1) / steps, world)
+        dist_barrier(world)
+    if rank == 0:
+        print(json.dumps({
+            "metric": "R8F64 7680x4320 single-frame latency, row strips across GPUs", "value": ms, "unit": "ms",
+            "n_gpus": world, "steps": steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": False,
+            "scaling": "strong", "vs_baseline": None, "dtype": "fp16", "data": "synthetic",
+            "config": {"workload": "C4 (second part): one 7680x4320 luma frame, R8F64",
+                       "split": f"{world} row strips, {halo}-row recompute halo each side, no exchange",
+                       "strip_rows_rank0": st.rows}}))
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -214,10 +278,15 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=None)
     ap.add_argument("--e2e-engines", type=int, default=2)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--frame-split", action="store_true",
+                    help="BASELINE config 4, second part: one 7680x4320 R8F64 frame split into row "
+                         "strips across the ranks (strip latency, max over ranks)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     if args.impl == "reference":
         return run_reference(args)
+    if args.frame_split:
+        return run_frame_split(args)
 
     import tempfile
 
