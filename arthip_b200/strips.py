@@ -33,9 +33,11 @@ class Strip:
         return self.in_hi - self.in_lo
 
 
-def conv_depth(engine) -> int:
-    """Number of 3x3 convs on the path, i.e. the receptive-field radius in rows."""
-    return sum(1 for o in engine.ops() if o["kind"].startswith("conv"))
+def conv_depth(model_path) -> int:
+    """Number of 3x3 convs on the model's path, i.e. the receptive-field radius in rows
+    (from the host-side parse and fusion, no GPU needed)."""
+    from .engine import inspect_model
+    return sum(1 for line in inspect_model(model_path)["ops"] if line.startswith("Conv"))
 
 
 def plan_strips(height: int, n: int, halo: int) -> list[Strip]:

@@ -125,6 +125,7 @@ def dist_setup(backend: str = "nccl"):
         import datetime
         import torch
         import torch.distributed as dist
+        os.environ.setdefault("NCCL_DEBUG", "WARN")  # stdout carries only the JSON line
         if backend == "nccl":
             torch.cuda.set_device(local)
             dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
@@ -228,7 +229,7 @@ def run_frame_split(args):
     with tempfile.TemporaryDirectory() as td:
         cm, path = build_model(Path(td))
         eng = Engine(path, device=local)
-        halo = conv_depth(eng)
+        halo = conv_depth(path)
         st = plan_strips(H8, world, halo)[rank]
         in_ptr, out_ptr, in_bytes, out_bytes = eng.prepare(1, st.rows, W8)
         frame = modelgen.synthetic_frame(seed, 1, H8, W8)

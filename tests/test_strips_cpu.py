@@ -22,3 +22,12 @@ def test_plan_covers_every_row_once_with_clamped_halos(height, n, halo):
 def test_plan_rejects_more_strips_than_rows():
     with pytest.raises(ValueError):
         plan_strips(3, 4, 1)
+
+
+def test_conv_depth_of_r8f64_is_18(tmp_path):
+    from arthip_b200 import modelgen, onnx_proto as op
+    from arthip_b200.strips import conv_depth
+    cm = modelgen.conv_chain(modelgen.CONFIGS["R8F64"], seed=1)
+    p = tmp_path / "m.onnx"
+    op.save_model(cm.model, p)
+    assert conv_depth(p) == 18

@@ -22,7 +22,7 @@ def test_strips_stitch_to_the_whole_frame(tmp_path, n):
     x = modelgen.synthetic_frame(4, 1, 270, 480)
     eng = Engine(p)
     full = eng.run(x)
-    halo = conv_depth(eng)
+    halo = conv_depth(p)
     assert halo == 18
     parts = [run_strip(eng, x, s, 2) for s in plan_strips(270, n, halo)]
     np.testing.assert_array_equal(stitch(parts), full)
