@@ -942,7 +942,6 @@ bool Engine::EnsureBuilt(const std::vector<int64_t>& s4, std::string& error) {
           to.clip = d.sout.clip;
           to.clip_lo = d.sout.clip_lo;
           to.clip_hi = d.sout.clip_hi;
-          to.single_pipe = o.adds.size() >= 2 ? 1 : 0;  // two residual operands: one pipeline is faster
           std::string perr;
           if (!conv_tc_plan(&cw.tcw, static_cast<const __half*>(bufs_[d.in_buf]), d.H, d.W, to, num_sms_, &d.tc,
                             &perr)) {

@@ -105,21 +105,21 @@ int slot_bytes_of(const ConvTcWeights* w) {
 // Shared memory of a plan: weights + row slots + ones/bias tiles + staging + tail.
 // Staging bytes of one epilogue warp: the standard kernel's 8 warps take alternate 32-channel
 // groups; the vertical-window kernel's 4 warps per pipe take every group of their quarter.
-int stage_per_warp_of(int MT, bool dual, int mode) {
+int stage_per_warp_of(int MT, bool vert, int mode) {
   if (mode != 0) return 0;
   const int ngroups = (MT + 31) / 32;
-  return (dual ? ngroups : (ngroups + 1) / 2) * kStageTile;
+  return (vert ? ngroups : (ngroups + 1) / 2) * kStageTile;
 }
 
 // Shared memory of a plan: weights + row slots (per pipe: two pipes in the vertical-window
 // kernel) + ones/bias tiles + staging + tail.
-int smem_need(const ConvTcWeights* w, int MT, bool vert, int mode, int slots, bool dual) {
+int smem_need(const ConvTcWeights* w, int MT, bool vert, int mode, int slots) {
   int wb = 0;
   for (int b = 0; b < (vert ? 3 : 9); ++b)
     for (int k = 0; k < w->nchunks; ++k) wb += round_up((vert ? 3 : 1) * MT * w->chunk[k].rowbytes, 1024);
-  const int pipes = dual ? 2 : 1;
+  const int pipes = vert ? 2 : 1;
   return wb + pipes * slots * slot_bytes_of(w) + 4096 + round_up(MT * 32, 1024) +
-         kEpiWarps * stage_per_warp_of(MT, dual, mode) + kTailBytes + 1024;
+         kEpiWarps * stage_per_warp_of(MT, vert, mode) + kTailBytes + 1024;
 }
 
 }  // namespace
@@ -133,7 +133,7 @@ size_t conv_tc_pack_layout(int C, int M, ConvTcWeights* L) {
   // MMA and a power-of-two ring of Mpad-column chunks) and its weights plus 3 row slots
   // resident in shared memory.
   const int Mp = L->Mpad;
-  L->vert = ((Mp == 16 || Mp == 32 || Mp == 64) && smem_need(L, Mp, true, 0, 3, true) <= kSmemLimit) ? 1 : 0;
+  L->vert = ((Mp == 16 || Mp == 32 || Mp == 64) && smem_need(L, Mp, true, 0, 3) <= kSmemLimit) ? 1 : 0;
   const int nblk = L->vert ? 3 : 9;
   const int rows = L->vert ? 3 * Mp : Mp;
   long long off = 0;
@@ -218,12 +218,11 @@ bool conv_tc_plan(const ConvTcWeights* w, const __half* in, int H, int W, const 
   const int slot_bytes = slot_bytes_of(w);
   P->slot_bytes = slot_bytes;
   const bool vert = w->vert != 0;
-  const bool dual = vert && !(out.single_pipe && out.mode == 0);
   int chosen = 0, slots = 0;
   if (vert) {
     // Whole output-channel range per CTA; deepest input-row ring that fits.
     for (int s = kMaxSlots; s >= 3 && !chosen; --s)
-      if (smem_need(w, w->Mpad, true, out.mode, s, dual) <= kSmemLimit) {
+      if (smem_need(w, w->Mpad, true, out.mode, s) <= kSmemLimit) {
         chosen = w->Mpad;
         slots = s;
       }
@@ -238,7 +237,7 @@ bool conv_tc_plan(const ConvTcWeights* w, const __half* in, int H, int W, const 
       for (int ns = nsplit + 1; ns <= w->Mpad / 16; ++ns)
         if (w->Mpad % ns == 0 && (w->Mpad / ns) % 16 == 0) can_split = true;
       for (int s = kMaxSlots; s >= 3; --s) {
-        if (smem_need(w, MT, false, out.mode, s, false) <= kSmemLimit) {
+        if (smem_need(w, MT, false, out.mode, s) <= kSmemLimit) {
           if (s < 4 && can_split) break;  // rather split the channels than run a 3-slot ring
           chosen = MT;
           slots = s;
@@ -252,7 +251,6 @@ bool conv_tc_plan(const ConvTcWeights* w, const __half* in, int H, int W, const 
     return false;
   }
   P->vert = vert ? 1 : 0;
-  P->dual = dual ? 1 : 0;
   P->MT = chosen;
   P->n_msplit = w->Mpad / chosen;
   P->nslots = slots;
@@ -263,26 +261,21 @@ bool conv_tc_plan(const ConvTcWeights* w, const __half* in, int H, int W, const 
       off += round_up((vert ? 3 : 1) * chosen * w->chunk[k].rowbytes, 1024);
     }
   P->w_smem_bytes = off;
-  off += (dual ? 2 : 1) * slots * slot_bytes;
+  off += (vert ? 2 : 1) * slots * slot_bytes;
   P->ones_off = off;
   off += 4096;
   P->biasb_off = off;
   off += round_up(chosen * 32, 1024);
   P->stage_off = off;
-  P->stage_per_warp = stage_per_warp_of(chosen, dual, out.mode);
+  P->stage_per_warp = stage_per_warp_of(chosen, vert, out.mode);
   off += kEpiWarps * P->stage_per_warp;
   P->smem_bytes = static_cast<size_t>(off) + kTailBytes + 1024;
-  if (dual) {
+  if (vert) {
     // Two pipes, each with half of the 512 TMEM columns as a ring of chunks of M columns
     // (a power of two, at most kMaxAcc of them), one per output row in flight.
     P->acc_stride = chosen;
     P->nacc = std::min(256 / chosen, kMaxAcc);
     P->tmem_cols = 512;
-  } else if (vert) {
-    // One pipe: the whole TMEM as the ring.
-    P->acc_stride = chosen;
-    P->nacc = std::min(512 / chosen, kMaxAcc);
-    P->tmem_cols = P->nacc * chosen;
   } else {
     P->acc_stride = round_up(chosen, 32);
     P->nacc = (4 * P->acc_stride <= 512) ? 4 : 2;
@@ -308,8 +301,7 @@ bool conv_tc_plan(const ConvTcWeights* w, const __half* in, int H, int W, const 
   static std::unordered_set<const void*> attr_set;
   std::lock_guard<std::mutex> lock(mu);
   for (int v = 0; v < kVariants; ++v) {
-    if (vert && !dual && v > 2) break;  // one-pipe vertical kernels: NHWC output only
-    KernelFn fn = kernel_for(w->C, vert, v, dual);
+    KernelFn fn = kernel_for(w->C, vert, v);
     if (attr_set.count(reinterpret_cast<const void*>(fn))) continue;
     cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
     if (e != cudaSuccess) {
@@ -386,8 +378,7 @@ cudaError_t conv_tc_launch(const ConvTcPlan& P, const __half* add1, const __half
     variant = 3;
   }
   dim3 grid(P.grid_x, P.n_msplit);
-  kernel_for(w->C, P.vert != 0, variant, P.dual != 0)<<<grid, P.dual ? kThreads2 : kThreads, P.smem_bytes,
-                                                      stream>>>(a);
+  kernel_for(w->C, P.vert != 0, variant)<<<grid, P.vert ? kThreads2 : kThreads, P.smem_bytes, stream>>>(a);
   return cudaGetLastError();
 }
 
@@ -396,25 +387,25 @@ cudaError_t conv_tc_launch(const ConvTcPlan& P, const __half* add1, const __half
 namespace ah {
 namespace tck {
 
-KernelFn kernel_c16(bool vert, int variant, bool dual);
-KernelFn kernel_c32(bool vert, int variant, bool dual);
-KernelFn kernel_c48(bool vert, int variant, bool dual);
-KernelFn kernel_c64(bool vert, int variant, bool dual);
-KernelFn kernel_c80(bool vert, int variant, bool dual);
-KernelFn kernel_c96(bool vert, int variant, bool dual);
-KernelFn kernel_c112(bool vert, int variant, bool dual);
-KernelFn kernel_c128(bool vert, int variant, bool dual);
+KernelFn kernel_c16(bool vert, int variant);
+KernelFn kernel_c32(bool vert, int variant);
+KernelFn kernel_c48(bool vert, int variant);
+KernelFn kernel_c64(bool vert, int variant);
+KernelFn kernel_c80(bool vert, int variant);
+KernelFn kernel_c96(bool vert, int variant);
+KernelFn kernel_c112(bool vert, int variant);
+KernelFn kernel_c128(bool vert, int variant);
 
-KernelFn kernel_for(int C, bool vert, int variant, bool dual) {
+KernelFn kernel_for(int C, bool vert, int variant) {
   switch (C) {
-    case 16: return kernel_c16(vert, variant, dual);
-    case 32: return kernel_c32(vert, variant, dual);
-    case 48: return kernel_c48(vert, variant, dual);
-    case 64: return kernel_c64(vert, variant, dual);
-    case 80: return kernel_c80(vert, variant, dual);
-    case 96: return kernel_c96(vert, variant, dual);
-    case 112: return kernel_c112(vert, variant, dual);
-    default: return kernel_c128(vert, variant, dual);
+    case 16: return kernel_c16(vert, variant);
+    case 32: return kernel_c32(vert, variant);
+    case 48: return kernel_c48(vert, variant);
+    case 64: return kernel_c64(vert, variant);
+    case 80: return kernel_c80(vert, variant);
+    case 96: return kernel_c96(vert, variant);
+    case 112: return kernel_c112(vert, variant);
+    default: return kernel_c128(vert, variant);
   }
 }
 

@@ -5,7 +5,7 @@
 namespace ah {
 namespace tck {
 
-KernelFn kernel_c112(bool vert, int variant, bool dual) { return pick<1, 1, 1>(vert, variant, dual); }
+KernelFn kernel_c112(bool vert, int variant) { return pick<1, 1, 1>(vert, variant); }
 
 }  // namespace tck
 }  // namespace ah

@@ -5,7 +5,7 @@
 namespace ah {
 namespace tck {
 
-KernelFn kernel_c128(bool vert, int variant, bool dual) { return pick<2, 0, 0>(vert, variant, dual); }
+KernelFn kernel_c128(bool vert, int variant) { return pick<2, 0, 0>(vert, variant); }
 
 }  // namespace tck
 }  // namespace ah

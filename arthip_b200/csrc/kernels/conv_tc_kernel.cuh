@@ -24,22 +24,23 @@
 //    groups): tcgen05.ld -> fp16 rounding (the conv node output) -> ReLU / SiLU -> up to
 //    two residual adds (fp16 adds, as the ONNX Add nodes) -> output.
 //
-// Two MMA formulations (VERT):
-//  * standard: per output row, 9 taps x C/16 MMAs of 128 x MT x 16;
-//  * vertical window (Mpad = 16, 32, 64): an input row feeds output rows j, j-1, j-2
-//    through kernel rows ky = 0, 1, 2; the weights of a (kx, chunk) block hold the three
-//    kernel rows stacked along N, and the three output rows sit in consecutive chunks of
-//    a TMEM ring, so one MMA of N = 3M per (kx, k-block) does all three.
+// Two MMA formulations:
+//  * standard (conv3x3_tc_kernel): per output row, 9 taps x C/16 MMAs of 128 x MT x 16;
+//  * vertical window (conv3x3_tc_vert2_kernel, Mpad = 16, 32, 64): an input row feeds
+//    output rows j, j-1, j-2 through kernel rows ky = 0, 1, 2; the weights of a
+//    (kx, chunk) block hold the three kernel rows stacked along N, and the three output
+//    rows sit in consecutive chunks of a TMEM ring, so one MMA of N = 3M per
+//    (kx, k-block) does all three. It runs two row pipelines per CTA (below).
 // Three output forms (EPI): 0 = NHWC fp16 through a swizzled staging tile and TMA stores;
 // 1 = 2x DepthToSpace (DCR) into NCHW with paired stores (upscaler tails); 2 = general
 // per-element DepthToSpace / clip / fp32 / layout stores.
 //
-// Every variant is a separate instantiation (chunk geometry x VERT x EPI x ACT), so each
-// kernel's code holds only its own path: runtime switches in the per-row loops and their
-// code size cost more than the work they select.
+// Every variant is a separate instantiation (chunk geometry x formulation x EPI x ACT), so
+// each kernel's code holds only its own path: runtime switches in the per-row loops and
+// their code size cost more than the work they select.
 //
-// Warp roles (320 threads): warp 0 = TMA producer, warp 1 = TMEM allocator + MMA issuer
-// (one thread), warps 2..9 = epilogue. Work: the (strip, row) space is split into
+// Warp roles of the standard kernel (320 threads): warp 0 = TMA producer, warp 1 = TMEM
+// allocator + MMA issuer (one thread), warps 2..9 = epilogue. Work: the (strip, row) space is split into
 // contiguous ranges, one per CTA; every pipeline wait is time-bounded.
 #pragma once
 
@@ -94,10 +95,9 @@ struct ConvTcArgs {
 typedef void (*KernelFn)(ConvTcArgs);
 
 // The instantiation for an input channel count (C % 16 == 0, 16 <= C <= 128), a
-// formulation (vertical window with two pipelines, or one pipeline), and an output variant
-// (0-2: NHWC with act none/relu/silu, 3: 2x DepthToSpace tail, 4: general per-element
-// output; the one-pipeline vertical kernel exists for 0-2 only).
-KernelFn kernel_for(int C, bool vert, int variant, bool dual);
+// formulation (vertical window, or standard) and an output variant (0-2: NHWC with act
+// none/relu/silu, 3: 2x DepthToSpace tail, 4: general per-element output).
+KernelFn kernel_for(int C, bool vert, int variant);
 
 struct Segment {
   int strip, ya, yb;
@@ -245,7 +245,7 @@ __device__ __forceinline__ void vert_row_mmas(uint32_t sl, const uint32_t (&bv)[
   }
 }
 
-template <int NC64, int NC32, int NC16, bool VERT, int EPI, int ACT>
+template <int NC64, int NC32, int NC16, int EPI, int ACT>
 __global__ void __launch_bounds__(kThreads, 1) conv3x3_tc_kernel(const __grid_constant__ ConvTcArgs a) {
   using Cfg = ChunkCfg<NC64, NC32, NC16>;
   extern __shared__ uint8_t smem_raw[];
@@ -320,9 +320,9 @@ __global__ void __launch_bounds__(kThreads, 1) conv3x3_tc_kernel(const __grid_co
   if (warp == 0) {
     // ---------------- TMA producer ----------------
     if (lane == 0) {
-      // weight blocks: 9 taps x chunks of MT rows, or (vertical) 3 kx x chunks of 3M rows
-      constexpr int nblk = (VERT ? 3 : 9) * Cfg::N;
-      const int wrows = VERT ? 3 * a.MT : a.MT;
+      // weight blocks: 9 taps x chunks of MT rows
+      constexpr int nblk = 9 * Cfg::N;
+      const int wrows = a.MT;
       uint32_t wbytes = 0;
 #pragma unroll
       for (int idx = 0; idx < nblk; ++idx) wbytes += wrows * Cfg::rb(idx % Cfg::N);
@@ -372,105 +372,53 @@ __global__ void __launch_bounds__(kThreads, 1) conv3x3_tc_kernel(const __grid_co
       bool ok = ptx::mbar_wait(ptx::smem_u32(wbar), 0, abort_flag, a.wait_limit_ns);
       SegIter it{t0, t1, a.H};
       Segment sg;
-      if constexpr (VERT) {
-        // Input row j of a segment feeds output rows j, j-1, j-2 through kernel rows
-        // ky = 0, 1, 2. Output row o lives in TMEM chunk ring(o) of M columns
-        // (ring(o) = -o mod NCH), so those outputs occupy consecutive chunks and the three
-        // kernel rows (stacked along N in the weight block) go out as one MMA of N = 3M
-        // (split in two where the window wraps around the ring).
-        const uint32_t M = a.MT, NCH = a.nacc;
-        const uint32_t idM = ptx::idesc_f16_f32(kTcTilePx, M);
-        // Low descriptor words of the weight block of every (kx, chunk); the A operand of
-        // a slot is its base word plus a compile-time offset (all shared addresses are
-        // below 256 KB, so adding to the 14-bit start field never carries).
-        uint32_t bv[3][Cfg::N];
+      const uint32_t idesc = ptx::idesc_f16_f32(kTcTilePx, a.MT);
+      uint32_t blo[9][Cfg::N];
 #pragma unroll
-        for (int kx = 0; kx < 3; ++kx)
+      for (int t = 0; t < 9; ++t)
 #pragma unroll
-          for (int k = 0; k < Cfg::N; ++k) bv[kx][k] = ptx::desc_lo(sW_u + a.wofs[kx * Cfg::N + k]);
-        uint32_t obase = 0;
-        RingPos fp;
-        while (ok && it.next(sg)) {
-          const int n = sg.yb - sg.ya;
-          for (int j = 0; j <= n + 1 && ok; ++j, fp.step(S)) {
-            const uint32_t slot = fp.slot;
-            ok = ptx::mbar_wait(ptx::smem_u32(&full[slot]), fp.phase, abort_flag, a.wait_limit_ns);
-            const int ky_lo = max(0, j - (n - 1)), ky_hi = min(2, j);
-            if (ok && ky_lo == 0) {  // output row j starts here: bias-initialise its chunk
-              const uint32_t o = obase + j, c = (NCH - (o & (NCH - 1))) & (NCH - 1);
-              ok = ptx::mbar_wait(ptx::smem_u32(&acce[c]), ((o >> lgA) & 1u) ^ 1u, abort_flag, a.wait_limit_ns);
-              ptx::tc_fence_after();
-              if (ok) ptx::mma_f16_ss(tmem_base + c * M, ones_desc, biasb_desc, idM, 0);
-            }
-            if (!ok) break;
-            const uint32_t ohi = obase + j - ky_lo;
-            const uint32_t chi = (NCH - (ohi & (NCH - 1))) & (NCH - 1);
-            const uint32_t span = ky_hi - ky_lo + 1;
-            const uint32_t n1 = min(span, NCH - chi), n2 = span - n1;
-            const uint32_t d1 = tmem_base + chi * M, d2 = tmem_base;
-            const uint32_t i1 = ptx::idesc_f16_f32(kTcTilePx, n1 * M), i2 = ptx::idesc_f16_f32(kTcTilePx, n2 * M);
-            const uint32_t sl = alo0 + slot * slot16;
-            // One branch per row, none per MMA: a branch in the issue stream costs more than
-            // the MMA it guards.
-            if (n2 == 0) vert_row_mmas<Cfg, false>(sl, bv, M, ky_lo, n1, d1, d2, i1, i2);
-            else vert_row_mmas<Cfg, true>(sl, bv, M, ky_lo, n1, d1, d2, i1, i2);
-            ptx::mma_commit(ptx::smem_u32(&empty[slot]));
-            if (ky_hi == 2) {  // output row j-2 received its last kernel row
-              const uint32_t o = obase + j - 2, c = (NCH - (o & (NCH - 1))) & (NCH - 1);
-              ptx::mma_commit(ptx::smem_u32(&accf[c]));
-            }
-          }
-          obase += n;
+        for (int k = 0; k < Cfg::N; ++k) blo[t][k] = ptx::desc_lo(sW_u + a.wofs[t * Cfg::N + k]);
+      uint32_t acc_cnt = 0;
+      RingPos rp;  // ring position of the next input row to wait for
+      while (ok && it.next(sg)) {
+        const int n = sg.yb - sg.ya;
+        uint32_t slot[3];
+        for (int ky = 0; ky < 2 && ok; ++ky, rp.step(S)) {  // the first two rows of the segment
+          slot[ky] = rp.slot;
+          ok = ptx::mbar_wait(ptx::smem_u32(&full[slot[ky]]), rp.phase, abort_flag, a.wait_limit_ns);
         }
-      } else {
-        const uint32_t idesc = ptx::idesc_f16_f32(kTcTilePx, a.MT);
-        uint32_t blo[9][Cfg::N];
-#pragma unroll
-        for (int t = 0; t < 9; ++t)
-#pragma unroll
-          for (int k = 0; k < Cfg::N; ++k) blo[t][k] = ptx::desc_lo(sW_u + a.wofs[t * Cfg::N + k]);
-        uint32_t acc_cnt = 0;
-        RingPos rp;  // ring position of the next input row to wait for
-        while (ok && it.next(sg)) {
-          const int n = sg.yb - sg.ya;
-          uint32_t slot[3];
-          for (int ky = 0; ky < 2 && ok; ++ky, rp.step(S)) {  // the first two rows of the segment
-            slot[ky] = rp.slot;
-            ok = ptx::mbar_wait(ptx::smem_u32(&full[slot[ky]]), rp.phase, abort_flag, a.wait_limit_ns);
-          }
-          for (int i = 0; i < n && ok; ++i) {
-            // rows i and i+1 of the segment were waited for already; wait for row i+2
-            slot[2] = rp.slot;
-            ok = ptx::mbar_wait(ptx::smem_u32(&full[slot[2]]), rp.phase, abort_flag, a.wait_limit_ns);
-            rp.step(S);
-            const uint32_t acc = acc_cnt & (NACC - 1);
-            if (ok) ok = ptx::mbar_wait(ptx::smem_u32(&acce[acc]), ((acc_cnt >> lgA) & 1u) ^ 1u, abort_flag, a.wait_limit_ns);
-            if (!ok) break;
-            ptx::tc_fence_after();
-            const uint32_t d = tmem_base + acc * a.acc_stride;
-            ptx::mma_f16_ss(d, ones_desc, biasb_desc, idesc, 0);  // D = bias
-#pragma unroll
-            for (int ky = 0; ky < 3; ++ky) {
-              const uint32_t sl = alo0 + slot[ky] * slot16;
-#pragma unroll
-              for (int k = 0; k < Cfg::N; ++k)
-#pragma unroll
-                for (int kx = 0; kx < 3; ++kx)
-#pragma unroll
-                  for (int kb = 0; kb < Cfg::kblocks(k); ++kb)
-                    ptx::mma_f16_ss_acc(d, sl + ((Cfg::off(k) + kx * Cfg::rb(k) + kb * 32) >> 4), Cfg::hi(k),
-                                        blo[ky * 3 + kx][k] + kb * 2, Cfg::hi(k), idesc);
-            }
-            ptx::mma_commit(ptx::smem_u32(&accf[acc]));
-            ptx::mma_commit(ptx::smem_u32(&empty[slot[0]]));
-            slot[0] = slot[1];
-            slot[1] = slot[2];
-            ++acc_cnt;
-          }
+        for (int i = 0; i < n && ok; ++i) {
+          // rows i and i+1 of the segment were waited for already; wait for row i+2
+          slot[2] = rp.slot;
+          ok = ptx::mbar_wait(ptx::smem_u32(&full[slot[2]]), rp.phase, abort_flag, a.wait_limit_ns);
+          rp.step(S);
+          const uint32_t acc = acc_cnt & (NACC - 1);
+          if (ok) ok = ptx::mbar_wait(ptx::smem_u32(&acce[acc]), ((acc_cnt >> lgA) & 1u) ^ 1u, abort_flag, a.wait_limit_ns);
           if (!ok) break;
-          ptx::mma_commit(ptx::smem_u32(&empty[slot[0]]));  // the segment's last two rows
-          ptx::mma_commit(ptx::smem_u32(&empty[slot[1]]));
+          ptx::tc_fence_after();
+          const uint32_t d = tmem_base + acc * a.acc_stride;
+          ptx::mma_f16_ss(d, ones_desc, biasb_desc, idesc, 0);  // D = bias
+#pragma unroll
+          for (int ky = 0; ky < 3; ++ky) {
+            const uint32_t sl = alo0 + slot[ky] * slot16;
+#pragma unroll
+            for (int k = 0; k < Cfg::N; ++k)
+#pragma unroll
+              for (int kx = 0; kx < 3; ++kx)
+#pragma unroll
+                for (int kb = 0; kb < Cfg::kblocks(k); ++kb)
+                  ptx::mma_f16_ss_acc(d, sl + ((Cfg::off(k) + kx * Cfg::rb(k) + kb * 32) >> 4), Cfg::hi(k),
+                                      blo[ky * 3 + kx][k] + kb * 2, Cfg::hi(k), idesc);
+          }
+          ptx::mma_commit(ptx::smem_u32(&accf[acc]));
+          ptx::mma_commit(ptx::smem_u32(&empty[slot[0]]));
+          slot[0] = slot[1];
+          slot[1] = slot[2];
+          ++acc_cnt;
         }
+        if (!ok) break;
+        ptx::mma_commit(ptx::smem_u32(&empty[slot[0]]));  // the segment's last two rows
+        ptx::mma_commit(ptx::smem_u32(&empty[slot[1]]));
       }
       // Drain every issued MMA before the tensor memory is released.
       ptx::mma_commit(ptx::smem_u32(donebar));
@@ -497,9 +445,7 @@ __global__ void __launch_bounds__(kThreads, 1) conv3x3_tc_kernel(const __grid_co
       const int x = xw + lane;
       const bool valid = x < a.W;
       for (int y = sg.ya; y < sg.yb; ++y) {
-        // accumulator of this output row: ring position -o mod NACC in the vertical
-        // formulation (consecutive rows in descending chunks), o mod NACC otherwise
-        const uint32_t acc = VERT ? ((NACC - (acc_cnt & (NACC - 1))) & (NACC - 1)) : (acc_cnt & (NACC - 1));
+        const uint32_t acc = acc_cnt & (NACC - 1);  // accumulator of this output row
         const size_t pix = static_cast<size_t>(y) * a.W + (valid ? x : 0);
         if constexpr (EPI == 0) {
           // Residual lines of the row two ahead go to L2 now, so the register loads below
@@ -940,22 +886,27 @@ __global__ void __launch_bounds__(kThreads2, 1) conv3x3_tc_vert2_kernel(const __
             __syncwarp();
           }
         }
-        // Every channel group of this warp's lane quarter (M <= 64: at most 2 groups).
+        // Every channel group of this warp's lane quarter (M <= 64: at most 2 groups) is read
+        // out of TMEM first and the accumulator released at once: each pipe's ring has only
+        // one chunk beyond the three-row window, so the MMA issuer waits on this release.
+        uint32_t rrs[2][32];
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+          if (k >= ngroups) break;
+          const uint32_t taddr = tbase + (static_cast<uint32_t>(q * 32) << 16) + acc * M + k * 32;
+          if (min(32, a.MT - k * 32) == 32) ptx::tmem_ld_32x32b_x32(taddr, rrs[k]);
+          else ptx::tmem_ld_32x32b_x16(taddr, rrs[k]);
+        }
+        ptx::tmem_wait_ld();
+        ptx::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) ptx::mbar_arrive(ptx::smem_u32(&pacce[acc]));
 #pragma unroll
         for (int k = 0; k < 2; ++k) {
           const int g = k;
           if (g >= ngroups) break;
           const int cw = min(32, a.MT - g * 32);
-          uint32_t rr[32];
-          const uint32_t taddr = tbase + (static_cast<uint32_t>(q * 32) << 16) + acc * M + g * 32;
-          if (cw == 32) ptx::tmem_ld_32x32b_x32(taddr, rr);
-          else ptx::tmem_ld_32x32b_x16(taddr, rr);
-          ptx::tmem_wait_ld();
-          if (g + 1 >= ngroups) {  // last group read: release the accumulator
-            ptx::tc_fence_before();
-            __syncwarp();
-            if (lane == 0) ptx::mbar_arrive(ptx::smem_u32(&pacce[acc]));
-          }
+          const uint32_t (&rr)[32] = rrs[k];
           const int cbase = g * 32;
           if constexpr (EPI == 0) {
             uint8_t* st = stage + k * kStageTile;
@@ -1041,18 +992,10 @@ __global__ void __launch_bounds__(kThreads2, 1) conv3x3_tc_vert2_kernel(const __
   if (threadIdx.x == 0 && *abort_flag) atomicOr(a.status, 1u);
 }
 
-// All output variants of one chunk geometry: the standard formulation (conv3x3_tc_kernel),
-// the vertical window with two pipelines (conv3x3_tc_vert2_kernel) and with one
-// (conv3x3_tc_kernel, used for two-residual layers).
+// All output variants of one chunk geometry: the standard formulation (conv3x3_tc_kernel)
+// and the vertical window (conv3x3_tc_vert2_kernel).
 template <int NC64, int NC32, int NC16>
-KernelFn pick(bool vert, int variant, bool dual) {
-  if (vert && !dual) {
-    switch (variant) {
-      case 0: return conv3x3_tc_kernel<NC64, NC32, NC16, true, 0, kActNone>;
-      case 1: return conv3x3_tc_kernel<NC64, NC32, NC16, true, 0, kActRelu>;
-      default: return conv3x3_tc_kernel<NC64, NC32, NC16, true, 0, kActSilu>;
-    }
-  }
+KernelFn pick(bool vert, int variant) {
   if (vert) {
     switch (variant) {
       case 0: return conv3x3_tc_vert2_kernel<NC64, NC32, NC16, 0, kActNone>;
@@ -1063,11 +1006,11 @@ KernelFn pick(bool vert, int variant, bool dual) {
     }
   }
   switch (variant) {
-    case 0: return conv3x3_tc_kernel<NC64, NC32, NC16, false, 0, kActNone>;
-    case 1: return conv3x3_tc_kernel<NC64, NC32, NC16, false, 0, kActRelu>;
-    case 2: return conv3x3_tc_kernel<NC64, NC32, NC16, false, 0, kActSilu>;
-    case 3: return conv3x3_tc_kernel<NC64, NC32, NC16, false, 1, -1>;
-    default: return conv3x3_tc_kernel<NC64, NC32, NC16, false, 2, -1>;
+    case 0: return conv3x3_tc_kernel<NC64, NC32, NC16, 0, kActNone>;
+    case 1: return conv3x3_tc_kernel<NC64, NC32, NC16, 0, kActRelu>;
+    case 2: return conv3x3_tc_kernel<NC64, NC32, NC16, 0, kActSilu>;
+    case 3: return conv3x3_tc_kernel<NC64, NC32, NC16, 1, -1>;
+    default: return conv3x3_tc_kernel<NC64, NC32, NC16, 2, -1>;
   }
 }
 

@@ -62,9 +62,6 @@ struct ConvTcOut {
   int fp32 = 0;
   int clip = 0;
   float clip_lo = 0.f, clip_hi = 0.f;
-  // Vertical-window layers normally run two row pipelines per CTA; with two residual
-  // operands one pipeline is faster (measured), and the caller sets this (mode 0 only).
-  int single_pipe = 0;
 };
 
 // Per (layer, buffers, frame size) launch plan.
@@ -79,8 +76,7 @@ struct ConvTcPlan {
   int ones_off = 0, biasb_off = 0, stage_off = 0, stage_per_warp = 0;
   size_t smem_bytes = 0;
   int nacc = 0, acc_stride = 0, tmem_cols = 0;
-  int vert = 0;                // vertical-window MMA formulation (weights packed accordingly)
-  int dual = 0;                // vertical window with two row pipelines per CTA
+  int vert = 0;                // vertical window (two row pipelines per CTA; weights packed accordingly)
   int grid_x = 0;
   ConvTcOut out;
   CUtensorMap maps[kTcMaxChunks];
