@@ -125,7 +125,7 @@ def dist_setup(backend: str = "nccl"):
         import datetime
         import torch
         import torch.distributed as dist
-        os.environ.setdefault("NCCL_DEBUG", "WARN")  # stdout carries only the JSON line
+        os.environ["NCCL_DEBUG"] = "WARN"  # no NCCL banner: stdout carries only the JSON line
         if backend == "nccl":
             torch.cuda.set_device(local)
             dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
