@@ -377,9 +377,24 @@ cudaError_t conv_tc_launch(const ConvTcPlan& P, const __half* add1, const __half
              w->M <= 16 && w->M <= P.MT) {
     variant = 3;
   }
-  dim3 grid(P.grid_x, P.n_msplit);
-  kernel_for(w->C, P.vert != 0, variant)<<<grid, P.vert ? kThreads2 : kThreads, P.smem_bytes, stream>>>(a);
-  return cudaGetLastError();
+  // Programmatic dependent launch: this kernel's set-up (barriers, TMEM, weights) overlaps
+  // the previous kernel's last CTAs; it waits in hardware (griddepcontrol.wait) before it
+  // reads the previous layers' activations or writes its output. ARTHIP_NO_PDL=1 turns it off.
+  static const bool no_pdl = [] {
+    const char* v = std::getenv("ARTHIP_NO_PDL");
+    return v && *v == '1';
+  }();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(P.grid_x, P.n_msplit);
+  cfg.blockDim = dim3(P.vert ? kThreads2 : kThreads);
+  cfg.dynamicSmemBytes = P.smem_bytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = no_pdl ? 0 : 1;
+  return cudaLaunchKernelEx(&cfg, kernel_for(w->C, P.vert != 0, variant), a);
 }
 
 }  // namespace ah

@@ -268,6 +268,7 @@ __global__ void __launch_bounds__(kThreads, 1) conv3x3_tc_kernel(const __grid_co
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int m0 = blockIdx.y * a.MT;
+  ptx::griddep_launch_dependents();  // the next layer's CTAs may take SMs this grid frees
   const int S = a.nslots;
   const int NACC = a.nacc;  // a power of two
   const uint32_t lgA = 31 - __clz(static_cast<uint32_t>(NACC));
@@ -333,6 +334,7 @@ __global__ void __launch_bounds__(kThreads, 1) conv3x3_tc_kernel(const __grid_co
         const uint8_t* src = a.wpack + a.gofs[idx] + static_cast<long long>(m0) * Cfg::rb(k);
         ptx::bulk_load(ptx::smem_u32(sW + a.wofs[idx]), src, wrows * Cfg::rb(k), ptx::smem_u32(wbar));
       }
+      ptx::griddep_wait();  // the input rows come from the previous layer
       uint32_t g = 0;
       RingPos rp;
       SegIter it{t0, t1, a.H};
@@ -428,6 +430,7 @@ __global__ void __launch_bounds__(kThreads, 1) conv3x3_tc_kernel(const __grid_co
     __syncwarp();
   } else {
     // ---------------- epilogue (warps 2..9) ----------------
+    ptx::griddep_wait();  // residual operands and the output buffer belong to earlier layers
     const int e = warp - 2;
     const int q = warp & 3;   // tensor-memory lane quarter this warp may access
     const int half = e >> 2;  // this warp takes channel groups half, half+2, ...
@@ -639,6 +642,7 @@ __global__ void __launch_bounds__(kThreads2, 1) conv3x3_tc_vert2_kernel(const __
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  ptx::griddep_launch_dependents();  // the next layer's CTAs may take SMs this grid frees
   const int S = a.nslots;           // input-row slots per pipe
   const int NACC = a.nacc;          // accumulator chunks per pipe (a power of two)
   const uint32_t lgA = 31 - __clz(static_cast<uint32_t>(NACC));
@@ -714,6 +718,7 @@ __global__ void __launch_bounds__(kThreads2, 1) conv3x3_tc_vert2_kernel(const __
                          ptx::smem_u32(wbar));
         }
       }
+      ptx::griddep_wait();  // the input rows come from the previous layer
       uint64_t* pfull = full + pp * kMaxSlots;
       uint64_t* pempty = empty + pp * kMaxSlots;
       uint8_t* pA = sA + static_cast<size_t>(pp) * S * a.slot_bytes;
@@ -820,6 +825,7 @@ __global__ void __launch_bounds__(kThreads2, 1) conv3x3_tc_vert2_kernel(const __
     __syncwarp();
   } else {
     // ---------------- epilogue (warps 4..11) ----------------
+    ptx::griddep_wait();  // residual operands and the output buffer belong to earlier layers
     const int pp = (warp - 4) >> 2;  // pipe
     const int q = warp & 3;          // tensor-memory lane quarter this warp may access
     const int e = warp - 4;

@@ -132,6 +132,15 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
+// Programmatic dependent launch: a kernel launched with programmatic stream serialization
+// may start while the previous kernel in the stream is still running; `griddep_wait`
+// blocks until that kernel has completed and its memory is visible (hardware-managed, no
+// polling). `griddep_launch_dependents` lets the next kernel start as SMs free up.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // Bring the 128-byte line holding `p` into L2 (no register result, no completion).
 __device__ __forceinline__ void prefetch_l2(const void* p) {
   asm volatile("prefetch.global.L2 [%0];" ::"l"(reinterpret_cast<uint64_t>(p)));
