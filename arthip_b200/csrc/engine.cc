@@ -850,6 +850,22 @@ bool Engine::EnsureBuilt(const std::vector<int64_t>& s4, std::string& error) {
     const OpSpec& o = ops_[i];
     const int pi = static_cast<int>(i);
     const bool direct_here = out_direct && pi == out_op;
+    // In place: a conv whose last residual operand dies at this op writes its result over
+    // that operand (the tensor-core conv then adds the operand in L2 with reduce-add tile
+    // stores; the other conv kernels read each residual element before writing it). Not
+    // for the graph input, nor when the operand is also the conv's input or its first
+    // residual.
+    if (!direct_here && o.type == OpType::Conv && !o.adds.empty() && !o.fuse_dts && !o.fuse_clip &&
+        !tensor_buf_.count(o.out)) {
+      const std::string& r = o.adds.back();
+      const auto rb = tensor_buf_.find(r);
+      if (r != input_name_ && r != o.in0 && (o.adds.size() == 1 || o.adds[0] != r) && last_use.at(r) == pi &&
+          rb != tensor_buf_.end() && buf_bytes_[rb->second] >= static_cast<size_t>(Numel(shapes.at(o.out))) * 2) {
+        tensor_buf_[o.out] = rb->second;
+        auto lu = last_use.find(o.out);
+        buf_free_at[rb->second] = lu == last_use.end() ? pi : lu->second;
+      }
+    }
     if (!direct_here && alloc(o.out, pi) < 0) {
       DestroyShapeState();
       return false;

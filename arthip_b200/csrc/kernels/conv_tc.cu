@@ -326,6 +326,15 @@ cudaError_t conv_tc_launch(const ConvTcPlan& P, const __half* add1, const __half
   // The kernel takes a second residual operand only together with a first one.
   a.add1 = add1 ? add1 : add2;
   a.add2 = add1 ? add2 : nullptr;
+  // In place: when the NHWC output buffer is the last residual operand (the engine aliases
+  // them once that operand is dead), the epilogue does not load it; the tile stores become
+  // TMA reduce-adds, so L2 adds the operand: fp16(r + t) == fp16(t + r), the graph's Add.
+  const __half* last = a.add2 ? a.add2 : a.add1;
+  if (P.out.mode == 0 && last && static_cast<const void*>(last) == P.out.ptr) {
+    a.reduce_out = 1;
+    if (a.add2) a.add2 = nullptr;
+    else a.add1 = nullptr;
+  }
   a.status = status;
   a.out = P.out;
   for (int i = 0; i < 9 * w->nchunks; ++i) {

@@ -90,6 +90,9 @@ struct ConvTcArgs {
   // slot without loading it, so the MMA issuer's bounded wait for it runs out and the
   // kernel reports a timed-out wait in the status word instead of hanging.
   int stall_row;
+  // Output form 0 only: the output buffer already holds the layer's last residual operand,
+  // and the tile stores are TMA reduce-adds onto it (that operand is then not loaded).
+  int reduce_out;
 };
 
 typedef void (*KernelFn)(ConvTcArgs);
@@ -582,7 +585,9 @@ __global__ void __launch_bounds__(kThreads, 1) conv3x3_tc_kernel(const __grid_co
             for (int g = half, k = 0; g < ngroups; g += 2, ++k) {
               const int cw = min(32, a.MT - g * 32);
               const uint32_t src = ptx::smem_u32(stage + k * kStageTile);
-              ptx::tma_store_3d(cw == 32 ? &a.out_map32 : &a.out_map16, src, m0 + g * 32, xw, y);
+              const CUtensorMap* map = cw == 32 ? &a.out_map32 : &a.out_map16;
+              if (a.reduce_out) ptx::tma_reduce_add_3d(map, src, m0 + g * 32, xw, y);
+              else ptx::tma_store_3d(map, src, m0 + g * 32, xw, y);
             }
             ptx::bulk_commit_group();
           }
@@ -974,7 +979,9 @@ __global__ void __launch_bounds__(kThreads2, 1) conv3x3_tc_vert2_kernel(const __
             for (int g = 0; g < ngroups; ++g) {
               const int cw = min(32, a.MT - g * 32);
               const uint32_t src = ptx::smem_u32(stage + g * kStageTile);
-              ptx::tma_store_3d(cw == 32 ? &a.out_map32 : &a.out_map16, src, g * 32, xw, y);
+              const CUtensorMap* map = cw == 32 ? &a.out_map32 : &a.out_map16;
+              if (a.reduce_out) ptx::tma_reduce_add_3d(map, src, g * 32, xw, y);
+              else ptx::tma_store_3d(map, src, g * 32, xw, y);
             }
             ptx::bulk_commit_group();
           }

@@ -139,3 +139,43 @@ def test_timed_out_pipeline_wait_is_reported_and_recovers(monkeypatch):
     assert conv.status() == 0
     ref = torch_conv_layer(x, w, b, 1, [])
     assert_fp16_layer_close(out.float().cpu().numpy(), ref.cpu().numpy(), "after recovery", ref.abs().cpu().numpy())
+
+
+@pytest.mark.parametrize("C,M,H,W,act,nadds", [
+    (64, 64, 37, 300, 1, 1),    # vertical window, block conv B
+    (64, 64, 19, 131, 1, 2),    # block residual + global skip (only the last operand in place)
+    (32, 32, 9, 140, 1, 1),     # vertical window, 64B-swizzle chunk
+    (96, 96, 13, 150, 1, 1),    # standard formulation
+    (128, 128, 8, 140, 1, 1),   # channel-sliced launch
+    (64, 8, 11, 150, 0, 1),     # narrow N: per-element output form, in place but no reduce
+])
+def test_in_place_residual_is_bit_identical(C, M, H, W, act, nadds):
+    """Output buffer = the last residual operand (as the engine assigns it once that operand
+    is dead): the tensor-core conv then leaves the operand to reduce-add tile stores in L2.
+    The result must equal the out-of-place result bit for bit, including residuals in the
+    fp16 subnormal range behind ReLU zeros (no flush to zero in the L2 addition)."""
+    from arthip_b200.engine import Conv3x3
+    g = torch.Generator(device="cpu").manual_seed(C + M + H + nadds)
+    dev = torch.device("cuda:0")
+    x = torch.rand(1, H, W, C, generator=g).half().to(dev)
+    w = (torch.randn(M, C, 3, 3, generator=g) * (2.0 / (9 * C)) ** 0.5).numpy().astype(np.float16)
+    b = (torch.randn(M, generator=g) * 0.05).numpy().astype(np.float16)
+    adds = []
+    for _ in range(nadds):
+        r = torch.randn(1, H, W, M, generator=g)
+        tiny = torch.rand(1, H, W, M, generator=g) < 0.3
+        adds.append(torch.where(tiny, r * 3e-6, r).half().to(dev))
+    conv = Conv3x3(w, b.astype(np.float32), act=act)
+    s = torch.cuda.current_stream().cuda_stream
+    ref = torch.full((1, H, W, M), float("nan"), dtype=torch.float16, device=dev)
+    conv.run(x.data_ptr(), H, W, ref.data_ptr(), *(a.data_ptr() for a in adds), stream=s)
+    inplace = adds[-1].clone()
+    ops = [a.data_ptr() for a in adds[:-1]] + [inplace.data_ptr()]
+    conv.run(x.data_ptr(), H, W, inplace.data_ptr(), *ops, stream=s)
+    torch.cuda.synchronize()
+    assert conv.status() == 0
+    assert int((adds[-1].abs() < 6.1e-5).sum()) > 0
+    if act == 1:  # ReLU zeros leave subnormal residuals as results
+        assert int((ref.abs() < 6.1e-5).sum()) > 0
+    diff = (inplace.view(torch.int16) != ref.view(torch.int16))
+    assert int(diff.sum()) == 0, f"{int(diff.sum())} elements differ in place"
