@@ -932,7 +932,9 @@ bool Engine::EnsureBuilt(const std::vector<int64_t>& s4, std::string& error) {
         d.act = o.act;
         for (size_t k = 0; k < o.adds.size(); ++k) d.add_buf[k] = tensor_buf_.at(o.adds[k]);
         lab << " " << d.C << "->" << d.M << (o.act == kActRelu ? " relu" : (o.act == kActSilu ? " silu" : ""))
-            << (o.adds.empty() ? "" : (o.adds.size() == 1 ? " +add" : " +add+add")) << (o.fuse_dts ? " +dts" : "");
+            << (o.adds.empty() ? "" : (o.adds.size() == 1 ? " +add" : " +add+add"))
+            << (!o.adds.empty() && d.out_buf >= 0 && d.out_buf == d.add_buf[o.adds.size() - 1] ? " in place" : "")
+            << (o.fuse_dts ? " +dts" : "");
         d.info.flops = 2.0 * 9.0 * d.C * d.M * P;
         d.info.bytes = 2.0 * P * d.C + 2.0 * P * d.M * (1.0 + o.adds.size()) + 2.0 * (9.0 * d.C * d.M + d.M);
         // Output form shared by both conv kernels: fused DepthToSpace / clip, and the

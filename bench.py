@@ -454,7 +454,7 @@ def main():
                 "api": f"ah_engine_run (synchronous, pinned host buffers), {n_eng} engines on {n_eng} host threads"},
         "roofline": {"bound": "tensor", "achieved": achieved_tflops, "peak": peak_tf, "unit": "TFLOP/s",
                      "frac": achieved_tflops / peak_tf, "traffic": traffic,
-                     "kernel": "conv3x3_tc_kernel (tcgen05)", "launches_per_frame": len(tc),
+                     "kernel": "conv3x3_tc_vert2_kernel (tcgen05)", "launches_per_frame": len(tc),
                      "peak_source": f"{peak_src} bf16_tflops_sustained",
                      "frame_roofline_frac": roof_ms / frame_ms, "frame_roofline_ms": roof_ms},
         "kernel_share": {k: v / tot for k, v in share.items()},
