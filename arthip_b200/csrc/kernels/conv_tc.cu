@@ -335,6 +335,15 @@ cudaError_t conv_tc_launch(const ConvTcPlan& P, const __half* add1, const __half
     if (a.add2) a.add2 = nullptr;
     else a.add1 = nullptr;
   }
+  // The two-pipeline kernel TMA-loads the first remaining operand into its staging tiles
+  // (same tile geometry as the output stores); if a map cannot be made, it loads per lane.
+  if (P.vert && P.out.mode == 0 && a.add1) {
+    EncodeTiledFn enc = get_encode_fn();
+    bool good = enc != nullptr;
+    if (good && P.MT >= 32) good = encode(enc, &a.res_map32, a.add1, w->M, P.W, P.H, 32, 32, nullptr);
+    if (good && P.MT % 32 == 16) good = encode(enc, &a.res_map16, a.add1, w->M, P.W, P.H, 16, 32, nullptr);
+    a.res_tma = good ? 1 : 0;
+  }
   a.status = status;
   a.out = P.out;
   for (int i = 0; i < 9 * w->nchunks; ++i) {

@@ -65,6 +65,11 @@ struct ConvTcArgs {
   CUtensorMap maps[kTcMaxChunks];
   CUtensorMap out_map32;
   CUtensorMap out_map16;
+  // Maps over the first loaded residual operand with the output tiles' geometry (used when
+  // res_tma is set: the two-pipeline kernel then TMA-loads that operand into the staging
+  // tiles one row ahead instead of loading it per lane).
+  CUtensorMap res_map32;
+  CUtensorMap res_map16;
   const uint8_t* wpack;
   const float* bias;
   const __half* add1;
@@ -93,6 +98,7 @@ struct ConvTcArgs {
   // Output form 0 only: the output buffer already holds the layer's last residual operand,
   // and the tile stores are TMA reduce-adds onto it (that operand is then not loaded).
   int reduce_out;
+  int res_tma;
 };
 
 typedef void (*KernelFn)(ConvTcArgs);
@@ -642,7 +648,8 @@ __global__ void __launch_bounds__(kThreads2, 1) conv3x3_tc_vert2_kernel(const __
   uint64_t* acce = accf + 2 * kMaxAcc;         // [2][kMaxAcc]
   uint64_t* wbar = acce + 2 * kMaxAcc;
   uint64_t* donebar = wbar + 1;                // [2]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(donebar + 2);
+  uint64_t* rbar = donebar + 2;                // [kEpiWarps] residual tiles of the epilogue warps
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(rbar + kEpiWarps);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -668,6 +675,7 @@ __global__ void __launch_bounds__(kThreads2, 1) conv3x3_tc_vert2_kernel(const __
     ptx::mbar_init(ptx::smem_u32(wbar), 1);
     ptx::mbar_init(ptx::smem_u32(&donebar[0]), 1);
     ptx::mbar_init(ptx::smem_u32(&donebar[1]), 1);
+    for (int i = 0; i < kEpiWarps; ++i) ptx::mbar_init(ptx::smem_u32(&rbar[i]), 1);
     *abort_flag = 0;
     ptx::fence_mbar_init();
   }
@@ -846,17 +854,46 @@ __global__ void __launch_bounds__(kThreads2, 1) conv3x3_tc_vert2_kernel(const __
     Segment sg;
     bool ok = true;
     bool stores_pending = false;
+    // First residual operand through the staging tiles (output form 0): lane 0 TMA-loads
+    // the tile of the next row as soon as this row's store has read the staging, and the
+    // math adds it in place. res_row: the row whose tile is in flight or landed.
+    // Compiled into the no-activation NHWC variant only (the residual convs of these
+    // models have no activation): the ReLU / SiLU variants keep their registers.
+    const bool rt = EPI == 0 && ACT == kActNone && a.res_tma != 0;
+    const __half* lop1 = rt ? nullptr : a.add1;  // operands loaded per lane
+    uint32_t res_cnt = 0;
+    int res_row = -1;
+    bool res_inflight = false;
+    auto issue_res = [&](int xw_, int yy) {  // lane 0
+      uint32_t bytes = 0;
+      for (int g = 0; g < ngroups; ++g) bytes += min(32, a.MT - g * 32) * 64;
+      ptx::mbar_arrive_expect_tx(ptx::smem_u32(&rbar[e]), bytes);
+      for (int g = 0; g < ngroups; ++g) {
+        const CUtensorMap* map = min(32, a.MT - g * 32) == 32 ? &a.res_map32 : &a.res_map16;
+        ptx::tma_load_3d(ptx::smem_u32(stage + g * kStageTile), map, ptx::smem_u32(&rbar[e]), g * 32, xw_, yy);
+      }
+    };
     while (ok && it.next(sg)) {
       const int xw = sg.strip * kTcTilePx + q * 32;  // first pixel of this warp's 32
       const int x = xw + lane;
       const bool valid = x < a.W;
+      const bool wl = xw < a.W;  // this warp stores anything in this strip
       for (int y = sg.ya; y < sg.yb; ++y) {
         // accumulator of this output row: consecutive rows sit in descending chunks
         const uint32_t acc = (NACC - (acc_cnt & (NACC - 1))) & (NACC - 1);
         const size_t pix = static_cast<size_t>(y) * a.W + (valid ? x : 0);
         uint4 pre[2][2][4];  // [operand][channel group][8 channels]
         if constexpr (EPI == 0) {
-          if (valid && a.add1) {
+          if (rt && wl && res_row != y) {  // first row of a segment: request its tile now
+            if (lane == 0) {
+              if (stores_pending) ptx::bulk_wait_group_read0();
+              issue_res(xw, y);
+            }
+            __syncwarp();
+            res_row = y;
+            res_inflight = true;
+          }
+          if (valid && (lop1 || a.add2)) {
             // Residual lines of the row two ahead go to L2 now; this row's residual
             // operands are loaded into registers before the accumulator wait.
             if (y + 2 < sg.yb) {
@@ -864,7 +901,7 @@ __global__ void __launch_bounds__(kThreads2, 1) conv3x3_tc_vert2_kernel(const __
               for (int g2 = 0; g2 < 2; ++g2) {
                 if (g2 >= ngroups) break;
                 const size_t off = (pix + 2 * static_cast<size_t>(a.W)) * a.M + g2 * 32;
-                ptx::prefetch_l2(a.add1 + off);
+                if (lop1) ptx::prefetch_l2(lop1 + off);
                 if (a.add2) ptx::prefetch_l2(a.add2 + off);
               }
             }
@@ -876,7 +913,7 @@ __global__ void __launch_bounds__(kThreads2, 1) conv3x3_tc_vert2_kernel(const __
 #pragma unroll
               for (int i = 0; i < 4; ++i) {
                 if (i * 8 >= cw) break;
-                pre[0][g2][i] = __ldg(reinterpret_cast<const uint4*>(a.add1 + off + i * 8));
+                if (lop1) pre[0][g2][i] = __ldg(reinterpret_cast<const uint4*>(lop1 + off + i * 8));
                 if (a.add2) pre[1][g2][i] = __ldg(reinterpret_cast<const uint4*>(a.add2 + off + i * 8));
               }
             }
@@ -912,6 +949,15 @@ __global__ void __launch_bounds__(kThreads2, 1) conv3x3_tc_vert2_kernel(const __
         ptx::tc_fence_before();
         __syncwarp();
         if (lane == 0) ptx::mbar_arrive(ptx::smem_u32(&pacce[acc]));
+        if (rt && wl) {  // this row's residual tile in the staging
+          const bool r_ok = ptx::mbar_wait(ptx::smem_u32(&rbar[e]), res_cnt & 1u, abort_flag, a.wait_limit_ns);
+          if (!__all_sync(0xffffffffu, r_ok)) {
+            ok = false;
+            break;
+          }
+          ++res_cnt;
+          res_inflight = false;
+        }
 #pragma unroll
         for (int k = 0; k < 2; ++k) {
           const int g = k;
@@ -932,11 +978,15 @@ __global__ void __launch_bounds__(kThreads2, 1) conv3x3_tc_vert2_kernel(const __
                 h[i] = *reinterpret_cast<uint32_t*>(&v);
               }
               act8<ACT>(h);
-              if (valid && a.add1) {
+              uint4* sp = reinterpret_cast<uint4*>(st + swz_granule(lane, j8 >> 3, rb));
+              if (rt) {
+                hadd8v(h, *sp);
+                if (valid && a.add2) hadd8v(h, pre[1][k][j8 >> 3]);
+              } else if (valid && a.add1) {
                 hadd8v(h, pre[0][k][j8 >> 3]);
                 if (a.add2) hadd8v(h, pre[1][k][j8 >> 3]);
               }
-              *reinterpret_cast<uint4*>(st + swz_granule(lane, j8 >> 3, rb)) = make_uint4(h[0], h[1], h[2], h[3]);
+              *sp = make_uint4(h[0], h[1], h[2], h[3]);
             }
           } else if constexpr (EPI == 1) {
             if (valid) {
@@ -986,11 +1036,24 @@ __global__ void __launch_bounds__(kThreads2, 1) conv3x3_tc_vert2_kernel(const __
             ptx::bulk_commit_group();
           }
           stores_pending = true;
+          if (rt && wl && y + 1 < sg.yb) {  // next row's tile, once this store has read the staging
+            if (lane == 0) {
+              ptx::bulk_wait_group_read0();
+              issue_res(xw, y + 1);
+            }
+            __syncwarp();
+            res_row = y + 1;
+            res_inflight = true;
+          }
         }
         ++acc_cnt;
       }
     }
     if constexpr (EPI == 0) {
+      if (res_inflight) {  // only after an abort: let the requested tile land before exit
+        volatile int never_abort = 0;
+        ptx::mbar_wait(ptx::smem_u32(&rbar[e]), res_cnt & 1u, &never_abort, a.wait_limit_ns);
+      }
       if (lane == 0) ptx::bulk_wait_group0();
     }
     __syncwarp();
