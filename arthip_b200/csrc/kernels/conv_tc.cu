@@ -129,11 +129,19 @@ size_t conv_tc_pack_layout(int C, int M, ConvTcWeights* L) {
   L->C = C;
   L->M = M;
   L->Mpad = round_up(M, 16);
-  // The vertical-window formulation needs Mpad = 16, 32 or 64 (3 * Mpad <= 256 columns per
-  // MMA and a power-of-two ring of Mpad-column chunks) and its weights plus 3 row slots
-  // resident in shared memory.
+  // The vertical-window formulation takes slices of vmt = 16, 32, 48 or 64 output channels
+  // (3 * vmt <= 256 columns per MMA; a ring of four or more vmt-column chunks per pipe):
+  // the whole Mpad when it is one of those, else 64- or 48-channel slices, one per CTA row
+  // of the grid. The slice's weights and 3 input-row slots per pipe (2 when the channels
+  // are sliced: the standard form would slice them too) must fit in shared memory.
   const int Mp = L->Mpad;
-  L->vert = ((Mp == 16 || Mp == 32 || Mp == 64) && smem_need(L, Mp, true, 0, 3) <= kSmemLimit) ? 1 : 0;
+  int vmt = 0;
+  if (Mp == 16 || Mp == 32 || Mp == 48 || Mp == 64) vmt = Mp;
+  else if (Mp % 64 == 0) vmt = 64;
+  else if (Mp % 48 == 0) vmt = 48;
+  const int min_slots = (vmt && Mp > vmt) ? 2 : 3;
+  L->vert = (vmt && smem_need(L, vmt, true, 0, min_slots) <= kSmemLimit) ? 1 : 0;
+  L->vmt = L->vert ? vmt : 0;
   const int nblk = L->vert ? 3 : 9;
   const int rows = L->vert ? 3 * Mp : Mp;
   long long off = 0;
@@ -153,12 +161,17 @@ void conv_tc_pack_into(const uint16_t* w_oihw, const ConvTcWeights& L, uint8_t* 
     for (int k = 0; k < L.nchunks; ++k) {
       const ConvTcChunk& ch = L.chunk[k];
       uint8_t* blk = img + L.gofs[b * L.nchunks + k];
-      // standard: block b = tap, row = m; vertical: block b = kx, row = ky * Mpad + m
-      // (rows of the padding channels m >= M stay zero)
+      // standard: block b = tap, row = m; vertical: block b = kx, row = slice * 3 vmt +
+      // ky * vmt + (m - slice * vmt) (rows of the padding channels m >= M stay zero)
+      const int vmt = L.vmt;
       for (int r = 0; r < (L.vert ? 3 * Mp : M); ++r) {
-        const int m = L.vert ? r % Mp : r;
+        int m = r, tap = b;
+        if (L.vert) {
+          const int sl = r / (3 * vmt), rr = r - sl * 3 * vmt;
+          m = sl * vmt + rr % vmt;
+          tap = (rr / vmt) * 3 + b;
+        }
         if (m >= M) continue;
-        const int tap = L.vert ? (r / Mp) * 3 + b : b;
         for (int kk = 0; kk < ch.cw; ++kk) {
           const int c = ch.c0 + kk;
           const uint16_t v = w_oihw[(static_cast<size_t>(m) * C + c) * 9 + tap];
@@ -220,10 +233,11 @@ bool conv_tc_plan(const ConvTcWeights* w, const __half* in, int H, int W, const 
   const bool vert = w->vert != 0;
   int chosen = 0, slots = 0;
   if (vert) {
-    // Whole output-channel range per CTA; deepest input-row ring that fits.
-    for (int s = kMaxSlots; s >= 3 && !chosen; --s)
-      if (smem_need(w, w->Mpad, true, out.mode, s) <= kSmemLimit) {
-        chosen = w->Mpad;
+    // One channel slice per CTA row of the grid; deepest input-row ring that fits.
+    const int min_slots = w->Mpad > w->vmt ? 2 : 3;
+    for (int s = kMaxSlots; s >= min_slots && !chosen; --s)
+      if (smem_need(w, w->vmt, true, out.mode, s) <= kSmemLimit) {
+        chosen = w->vmt;
         slots = s;
       }
   } else {
@@ -274,7 +288,9 @@ bool conv_tc_plan(const ConvTcWeights* w, const __half* in, int H, int W, const 
     // Two pipes, each with half of the 512 TMEM columns as a ring of chunks of M columns
     // (a power of two, at most kMaxAcc of them), one per output row in flight.
     P->acc_stride = chosen;
-    P->nacc = std::min(256 / chosen, kMaxAcc);
+    int nacc = std::min(256 / chosen, kMaxAcc);
+    while (nacc & (nacc - 1)) nacc &= nacc - 1;
+    P->nacc = nacc;
     P->tmem_cols = 512;
   } else {
     P->acc_stride = round_up(chosen, 32);

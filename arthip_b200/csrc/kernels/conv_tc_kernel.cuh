@@ -660,6 +660,7 @@ __global__ void __launch_bounds__(kThreads2, 1) conv3x3_tc_vert2_kernel(const __
   const uint32_t lgA = 31 - __clz(static_cast<uint32_t>(NACC));
   const uint32_t M = a.MT;          // = Mpad: one chunk of M columns per output row
   const uint32_t half_cols = a.tmem_cols / 2;
+  const int m0 = blockIdx.y * a.MT;  // this CTA's slice of output channels
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < 2 * S; ++i) {
@@ -699,7 +700,7 @@ __global__ void __launch_bounds__(kThreads2, 1) conv3x3_tc_vert2_kernel(const __
     uint4* row = reinterpret_cast<uint4*>(sBiasB + r * 32);
     row[0] = make_uint4(0, 0, 0, 0);
     row[1] = make_uint4(0, 0, 0, 0);
-    *reinterpret_cast<__half*>(sBiasB + swz_granule(r, 0, 32)) = __float2half(a.bias[r]);
+    *reinterpret_cast<__half*>(sBiasB + swz_granule(r, 0, 32)) = __float2half(a.bias[m0 + r]);
   }
   ptx::fence_proxy_async_smem();  // the tensor core reads the generic writes above
   ptx::tc_fence_before();
@@ -727,7 +728,8 @@ __global__ void __launch_bounds__(kThreads2, 1) conv3x3_tc_vert2_kernel(const __
 #pragma unroll
         for (int idx = 0; idx < nblk; ++idx) {
           const int k = idx % Cfg::N;
-          ptx::bulk_load(ptx::smem_u32(sW + a.wofs[idx]), a.wpack + a.gofs[idx], wrows * Cfg::rb(k),
+          ptx::bulk_load(ptx::smem_u32(sW + a.wofs[idx]),
+                         a.wpack + a.gofs[idx] + static_cast<long long>(3 * m0) * Cfg::rb(k), wrows * Cfg::rb(k),
                          ptx::smem_u32(wbar));
         }
       }
@@ -870,7 +872,7 @@ __global__ void __launch_bounds__(kThreads2, 1) conv3x3_tc_vert2_kernel(const __
       ptx::mbar_arrive_expect_tx(ptx::smem_u32(&rbar[e]), bytes);
       for (int g = 0; g < ngroups; ++g) {
         const CUtensorMap* map = min(32, a.MT - g * 32) == 32 ? &a.res_map32 : &a.res_map16;
-        ptx::tma_load_3d(ptx::smem_u32(stage + g * kStageTile), map, ptx::smem_u32(&rbar[e]), g * 32, xw_, yy);
+        ptx::tma_load_3d(ptx::smem_u32(stage + g * kStageTile), map, ptx::smem_u32(&rbar[e]), m0 + g * 32, xw_, yy);
       }
     };
     while (ok && it.next(sg)) {
@@ -900,7 +902,7 @@ __global__ void __launch_bounds__(kThreads2, 1) conv3x3_tc_vert2_kernel(const __
 #pragma unroll
               for (int g2 = 0; g2 < 2; ++g2) {
                 if (g2 >= ngroups) break;
-                const size_t off = (pix + 2 * static_cast<size_t>(a.W)) * a.M + g2 * 32;
+                const size_t off = (pix + 2 * static_cast<size_t>(a.W)) * a.M + m0 + g2 * 32;
                 if (lop1) ptx::prefetch_l2(lop1 + off);
                 if (a.add2) ptx::prefetch_l2(a.add2 + off);
               }
@@ -909,7 +911,7 @@ __global__ void __launch_bounds__(kThreads2, 1) conv3x3_tc_vert2_kernel(const __
             for (int g2 = 0; g2 < 2; ++g2) {
               if (g2 >= ngroups) break;
               const int cw = min(32, a.MT - g2 * 32);
-              const size_t off = pix * a.M + g2 * 32;
+              const size_t off = pix * a.M + m0 + g2 * 32;
 #pragma unroll
               for (int i = 0; i < 4; ++i) {
                 if (i * 8 >= cw) break;
@@ -942,8 +944,14 @@ __global__ void __launch_bounds__(kThreads2, 1) conv3x3_tc_vert2_kernel(const __
         for (int k = 0; k < 2; ++k) {
           if (k >= ngroups) break;
           const uint32_t taddr = tbase + (static_cast<uint32_t>(q * 32) << 16) + acc * M + k * 32;
-          if (min(32, a.MT - k * 32) == 32) ptx::tmem_ld_32x32b_x32(taddr, rrs[k]);
-          else ptx::tmem_ld_32x32b_x16(taddr, rrs[k]);
+          if (min(32, a.MT - k * 32) < 32) {
+            ptx::tmem_ld_32x32b_x16(taddr, rrs[k]);
+          } else if (M & 31u) {  // 48-column chunks: 16-column loads at 16-aligned columns
+            ptx::tmem_ld_32x32b_x16(taddr, rrs[k]);
+            ptx::tmem_ld_32x32b_x16_hi(taddr + 16, rrs[k]);
+          } else {
+            ptx::tmem_ld_32x32b_x32(taddr, rrs[k]);
+          }
         }
         ptx::tmem_wait_ld();
         ptx::tc_fence_before();
@@ -1005,7 +1013,7 @@ __global__ void __launch_bounds__(kThreads2, 1) conv3x3_tc_vert2_kernel(const __
               const long long Ho = static_cast<long long>(a.H) * b, Wo = static_cast<long long>(a.W) * b;
 #pragma unroll
               for (int j = 0; j < 32; ++j) {
-                const int m = cbase + j;
+                const int m = m0 + cbase + j;
                 if (j >= cw || m >= a.M) break;
                 float t = act1(r16(__uint_as_float(rr[j])), act);
                 if (a.add1) t = r16(t + __half2float(a.add1[pix * a.M + m]));
@@ -1030,8 +1038,8 @@ __global__ void __launch_bounds__(kThreads2, 1) conv3x3_tc_vert2_kernel(const __
               const int cw = min(32, a.MT - g * 32);
               const uint32_t src = ptx::smem_u32(stage + g * kStageTile);
               const CUtensorMap* map = cw == 32 ? &a.out_map32 : &a.out_map16;
-              if (a.reduce_out) ptx::tma_reduce_add_3d(map, src, g * 32, xw, y);
-              else ptx::tma_store_3d(map, src, g * 32, xw, y);
+              if (a.reduce_out) ptx::tma_reduce_add_3d(map, src, m0 + g * 32, xw, y);
+              else ptx::tma_store_3d(map, src, m0 + g * 32, xw, y);
             }
             ptx::bulk_commit_group();
           }

@@ -37,11 +37,13 @@ struct ConvTcChunk {
 struct ConvTcWeights {
   int C = 0, M = 0;
   int Mpad = 0;                // M rounded up to 16 (zero weights and bias in the padding)
-  // Vertical-window packing (Mpad = 16, 32 or 64): one block per (kx, chunk) holding the
-  // three kernel rows ky stacked along N (3 * Mpad rows), so one MMA of N = 3 * Mpad serves
-  // the three output rows an input row feeds. Otherwise one block of Mpad rows per
-  // (tap, chunk).
+  // Vertical-window packing: the output channels form slices of vmt = 16, 32, 48 or 64
+  // (one slice per CTA row of the grid), and one block per (kx, chunk) holds, slice after
+  // slice, the three kernel rows ky stacked along N (3 * vmt rows per slice), so one MMA of
+  // N = 3 * vmt serves the three output rows an input row feeds. Otherwise one block of
+  // Mpad rows per (tap, chunk).
   int vert = 0;
+  int vmt = 0;
   int nchunks = 0;
   ConvTcChunk chunk[kTcMaxChunks];
   void* wpack = nullptr;       // device: swizzled K-major weight blocks (see vert)

@@ -48,7 +48,12 @@ def main(argv=None) -> int:
     ap.add_argument("--in-place", action="store_true",
                     help="write over the last residual operand (reduce-add stores); the "
                          "operand then accumulates across launches, which does not change the timing")
+    ap.add_argument("--model", choices=["C4F32", "R8F64", "R16F96"],
+                    help="time whole frames of this BASELINE chain (luma, 2x) at --H x --W through the "
+                         "engine's CUDA graph instead of one layer (a small-frame case for profilers)")
     args = ap.parse_args(argv)
+    if args.model:
+        return _model_frames(args)
 
     import torch
 
@@ -99,6 +104,45 @@ def main(argv=None) -> int:
     }))
     conv.close()
     return 0 if status == 0 else 1
+
+
+def _model_frames(args) -> int:
+    import tempfile
+    import time
+
+    import torch
+
+    from arthip_b200 import modelgen, onnx_proto as op
+    from arthip_b200.engine import Engine
+
+    H, W = args.H, args.W
+    with tempfile.TemporaryDirectory() as td:
+        cm = modelgen.conv_chain(modelgen.CONFIGS[args.model], seed=args.seed)
+        path = Path(td) / f"{args.model}.onnx"
+        op.save_model(cm.model, path)
+        eng = Engine(path)
+        in_ptr, _, in_bytes, _ = eng.prepare(1, H, W)
+        dev = torch.device("cuda:0")
+        frame = torch.from_numpy(modelgen.synthetic_frame(args.seed, 1, H, W).reshape(-1)).to(dev)
+        torch.cuda.synchronize()
+
+        class _B:  # the engine's input buffer as a torch view
+            __cuda_array_interface__ = {"shape": (in_bytes // 2,), "typestr": "<f2", "data": (in_ptr, False),
+                                        "version": 3}
+        torch.as_tensor(_B(), device=dev).copy_(frame)
+        torch.cuda.synchronize()
+        for _ in range(max(1, args.warmup)):
+            eng.enqueue()
+        eng.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(args.iters):
+            eng.enqueue()
+        eng.synchronize()
+        ms = (time.perf_counter() - t0) * 1e3 / args.iters
+        print(json.dumps({"model": f"{args.model} {H}x{W}", "ms_per_frame": ms, "fps": 1e3 / ms,
+                          "iters": args.iters, "timing": "host wall clock around enqueued graph replays"}))
+        eng.close()
+    return 0
 
 
 if __name__ == "__main__":

@@ -49,6 +49,18 @@ CFG = "R8F64"
 SEED = 2
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 WORKLOAD = "C2: ArtCNN-style R8F64 (18 conv3x3, ReLU, residual + global skip, DepthToSpace 2) fp16, 1920x1080 luma"
+TC_KERNEL = "conv3x3_tc_vert2_kernel (tcgen05)"
+# --config: C2 (the default and the reported line), or the other BASELINE configs timed the
+# same way: C3 (R16F96 at 1080p) and C4 (R8F64 at 2160p, per GPU).
+CONFIG_TABLE = {
+    "C2": (CFG, SEED, H, W, METRIC, WORKLOAD, TC_KERNEL),
+    "C3": ("R16F96", 3, 1080, 1920, "ArtCNN R16F96 fp16 fps @1080p per B200",
+           "C3: ArtCNN-style R16F96 (34 conv3x3, 96 channels, ReLU, residual + global skip, DepthToSpace 2) "
+           "fp16, 1920x1080 luma", "conv3x3_tc_kernel (tcgen05)"),
+    "C4": ("R8F64", 4, 2160, 3840, "ArtCNN R8F64 fp16 fps @2160p per B200",
+           "C4: ArtCNN-style R8F64 (18 conv3x3, ReLU, residual + global skip, DepthToSpace 2) fp16, 3840x2160 luma",
+           TC_KERNEL),
+}
 
 
 def load_peaks():
@@ -279,11 +291,15 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=None)
     ap.add_argument("--e2e-engines", type=int, default=2)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--config", default="C2", choices=sorted(CONFIG_TABLE),
+                    help="C2 (default): R8F64 1080p; C3: R16F96 1080p; C4: R8F64 2160p")
     ap.add_argument("--frame-split", action="store_true",
                     help="BASELINE config 4, second part: one 7680x4320 R8F64 frame split into row "
                          "strips across the ranks (strip latency, max over ranks)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
+    global CFG, SEED, H, W, METRIC, WORKLOAD, TC_KERNEL
+    CFG, SEED, H, W, METRIC, WORKLOAD, TC_KERNEL = CONFIG_TABLE[args.config]
     if args.impl == "reference":
         return run_reference(args)
     if args.frame_split:
@@ -420,7 +436,9 @@ def main():
     # DRAM bytes per tcgen05 conv launch from the committed one-pass ncu capture of this
     # workload (ncu cannot run inside a timed bench).
     traffic = None
-    tp = ROOT / "profiles" / "conv3x3_tc_kernel_traffic.json"
+    tp = ROOT / "profiles" / "conv3x3_tc_kernel_traffic.json"  # captured on C2
+    if args.config != "C2":
+        tp = ROOT / "profiles" / "no_capture_for_this_config"
     if tp.exists():
         try:
             traffic = json.loads(tp.read_text()).get("dram_bytes_per_launch")
@@ -454,7 +472,7 @@ def main():
                 "api": f"ah_engine_run (synchronous, pinned host buffers), {n_eng} engines on {n_eng} host threads"},
         "roofline": {"bound": "tensor", "achieved": achieved_tflops, "peak": peak_tf, "unit": "TFLOP/s",
                      "frac": achieved_tflops / peak_tf, "traffic": traffic,
-                     "kernel": "conv3x3_tc_vert2_kernel (tcgen05)", "launches_per_frame": len(tc),
+                     "kernel": TC_KERNEL, "launches_per_frame": len(tc),
                      "peak_source": f"{peak_src} bf16_tflops_sustained",
                      "frame_roofline_frac": roof_ms / frame_ms, "frame_roofline_ms": roof_ms},
         "kernel_share": {k: v / tot for k, v in share.items()},
