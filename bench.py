@@ -137,7 +137,10 @@ def dist_setup(backend: str = "nccl"):
         import datetime
         import torch
         import torch.distributed as dist
-        os.environ["NCCL_DEBUG"] = "WARN"  # no NCCL banner: stdout carries only the JSON line
+        # stdout carries only the JSON line: NCCL logs (its version line included, which it
+        # prints at every level from VERSION up) go to stderr.
+        os.environ["NCCL_DEBUG"] = "WARN"
+        os.environ["NCCL_DEBUG_FILE"] = "/dev/stderr"
         if backend == "nccl":
             torch.cuda.set_device(local)
             dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
