@@ -54,6 +54,11 @@ TC_CASES = [
     (32, 12, 7, 140, 1, 1),
     (48, 16, 33, 150, 2, 1),     # vertical window with N = 48 (chunks 32+16), SiLU, NHWC stores
     (64, 8, 40, 260, 0, 2),      # vertical window, padded N, per-element stores with two adds
+    (48, 48, 19, 200, 1, 0),     # vertical window, one 48-channel slice (N = 144)
+    (96, 96, 11, 140, 0, 1),     # two 48-channel slices; residual TMA-loaded into the staging
+    (96, 96, 7, 300, 0, 2),      # two slices, residual + global skip (first TMA-staged, second per lane)
+    (32, 96, 9, 131, 2, 0),      # two slices from a 32-channel input, SiLU
+    (64, 128, 10, 260, 0, 1),    # two 64-channel slices, staged residual
 ]
 
 
@@ -145,8 +150,9 @@ def test_timed_out_pipeline_wait_is_reported_and_recovers(monkeypatch):
     (64, 64, 37, 300, 1, 1),    # vertical window, block conv B
     (64, 64, 19, 131, 1, 2),    # block residual + global skip (only the last operand in place)
     (32, 32, 9, 140, 1, 1),     # vertical window, 64B-swizzle chunk
-    (96, 96, 13, 150, 1, 1),    # standard formulation
-    (128, 128, 8, 140, 1, 1),   # channel-sliced launch
+    (96, 96, 13, 150, 1, 1),    # vertical window in two 48-channel slices
+    (64, 128, 9, 140, 0, 2),    # two 64-channel slices, staged first operand, second in place
+    (128, 128, 8, 140, 1, 1),   # standard formulation, channel-sliced launch
     (64, 8, 11, 150, 0, 1),     # narrow N: per-element output form, in place but no reduce
 ])
 def test_in_place_residual_is_bit_identical(C, M, H, W, act, nadds):
