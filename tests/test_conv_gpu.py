@@ -59,6 +59,10 @@ TC_CASES = [
     (96, 96, 7, 300, 0, 2),      # two slices, residual + global skip (first TMA-staged, second per lane)
     (32, 96, 9, 131, 2, 0),      # two slices from a 32-channel input, SiLU
     (64, 128, 10, 260, 0, 1),    # two 64-channel slices, staged residual
+    (64, 4, 13, 300, 1, 0),      # narrow tail over three strips, partial last strip
+    (32, 3, 9, 253, 2, 1),       # narrow output with SiLU and a residual (per-element stores)
+    (16, 1, 5, 127, 0, 0),       # one output channel, one pixel short of a strip
+    (48, 5, 7, 130, 1, 0),       # five output channels, two pixels past a strip
 ]
 
 
