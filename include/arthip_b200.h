@@ -106,7 +106,11 @@ typedef struct ah_conv ah_conv;
  * act: 0 none, 1 ReLU, 2 SiLU. */
 int ah_conv3x3_create(int device, int C, int M, const uint16_t* w_oihw_f16, const float* bias, int act,
                       ah_conv** out, char* err, int errlen);
-/* Enqueue on `stream` (cudaStream_t, NULL = legacy default). add1/add2 may be NULL. */
+/* Enqueue on `stream` (cudaStream_t, NULL = legacy default). add1/add2 may be NULL; the
+ * result is ((conv + add1) + add2), each sum rounded to fp16. out_nhwc may be the same
+ * buffer as the last residual operand (an in-place residual update): the tensor-core
+ * kernel then leaves that addition to reduce-add tile stores in L2, with the same result
+ * bit for bit. It must not overlap in_nhwc. */
 int ah_conv3x3_run(ah_conv* c, const void* in_nhwc, int H, int W, const void* add1, const void* add2,
                    void* out_nhwc, void* stream, char* err, int errlen);
 /* 0 = tcgen05 tensor-core kernel, 1 = CUDA-core kernel. */
