@@ -232,9 +232,19 @@ bool conv_tc_plan(const ConvTcWeights* w, const __half* in, int H, int W, const 
   P->slot_bytes = slot_bytes;
   const bool vert = w->vert != 0;
   int chosen = 0, slots = 0;
+  bool dual = false;  // two CTAs per SM
   if (vert) {
     // One channel slice per CTA row of the grid; deepest input-row ring that fits.
     const int min_slots = w->Mpad > w->vmt ? 2 : 3;
+    // The 2x DepthToSpace tail (narrow N, little tensor work per row) is bound by its
+    // per-row MMA issue and epilogue chains, not by loads: it runs two CTAs per SM, each
+    // with two input slots per pipe and half of the tensor memory.
+    dual = out.mode == 1 && out.dts_b == 2 && (out.nchw || w->M == 4) && w->M % 4 == 0 && w->Mpad == 16 &&
+           smem_need(w, w->vmt, true, out.mode, 2) <= kSmemPerSm / 2 - 1024;
+    if (dual) {
+      chosen = w->vmt;
+      slots = 2;
+    }
     for (int s = kMaxSlots; s >= min_slots && !chosen; --s)
       if (smem_need(w, w->vmt, true, out.mode, s) <= kSmemLimit) {
         chosen = w->vmt;
@@ -285,13 +295,14 @@ bool conv_tc_plan(const ConvTcWeights* w, const __half* in, int H, int W, const 
   off += kEpiWarps * P->stage_per_warp;
   P->smem_bytes = static_cast<size_t>(off) + kTailBytes + 1024;
   if (vert) {
-    // Two pipes, each with half of the 512 TMEM columns as a ring of chunks of M columns
-    // (a power of two, at most kMaxAcc of them), one per output row in flight.
+    // Two pipes, each with half of the CTA's TMEM columns (all 512, or 256 with two CTAs
+    // per SM) as a ring of chunks of M columns (a power of two, at most kMaxAcc of them),
+    // one per output row in flight.
+    P->tmem_cols = dual ? 256 : 512;
     P->acc_stride = chosen;
-    int nacc = std::min(256 / chosen, kMaxAcc);
+    int nacc = std::min(P->tmem_cols / 2 / chosen, kMaxAcc);
     while (nacc & (nacc - 1)) nacc &= nacc - 1;
     P->nacc = nacc;
-    P->tmem_cols = 512;
   } else {
     P->acc_stride = round_up(chosen, 32);
     P->nacc = (4 * P->acc_stride <= 512) ? 4 : 2;
@@ -301,7 +312,7 @@ bool conv_tc_plan(const ConvTcWeights* w, const __half* in, int H, int W, const 
   }
   const long long n_strips = (W + kTcTilePx - 1) / kTcTilePx;
   const long long rows_total = n_strips * H;
-  long long gx = std::max(1, num_sms / P->n_msplit);
+  long long gx = std::max(1, (dual ? 2 : 1) * num_sms / P->n_msplit);
   if (gx > rows_total) gx = rows_total;
   P->grid_x = static_cast<int>(gx);
 

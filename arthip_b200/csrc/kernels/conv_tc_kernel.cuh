@@ -59,6 +59,7 @@ constexpr int kThreads = 64 + 32 * kEpiWarps;
 constexpr int kSmemLimit = 232448;  // 227 KB opt-in dynamic shared memory per block
 constexpr int kStageTile = 2048;    // one 32-pixel x 32-channel fp16 staging tile
 constexpr int kTailBytes = 1024;    // barriers and flags
+constexpr int kSmemPerSm = 233472;  // shared memory of one SM (two CTAs share it)
 constexpr int kVariants = 5;        // EPI 0 x ACT {none, relu, silu}; EPI 1; EPI 2
 
 struct ConvTcArgs {
@@ -632,7 +633,7 @@ __global__ void __launch_bounds__(kThreads, 1) conv3x3_tc_kernel(const __grid_co
 constexpr int kThreads2 = 384;
 
 template <int NC64, int NC32, int NC16, int EPI, int ACT>
-__global__ void __launch_bounds__(kThreads2, 1) conv3x3_tc_vert2_kernel(const __grid_constant__ ConvTcArgs a) {
+__global__ void __launch_bounds__(kThreads2, EPI == 1 ? 2 : 1) conv3x3_tc_vert2_kernel(const __grid_constant__ ConvTcArgs a) {
   using Cfg = ChunkCfg<NC64, NC32, NC16>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
