@@ -134,7 +134,7 @@ __global__ void __launch_bounds__(kHeadThreads) conv3x3_head_mma_kernel(const He
 #pragma unroll
             for (int i = 0; i < 2; ++i) {
               const float v = r16(acc[j][2 * r + i] + (i ? bias[j].y : bias[j].x));
-              o[i] = r16(v * r16(1.f / (1.f + expf(-v))));
+              o[i] = r16(v * r16(sigmoid_fast(v)));
             }
             h = __floats2half2_rn(o[0], o[1]);
           } else {

@@ -105,7 +105,7 @@ __global__ void __launch_bounds__(kSimtThreads) conv3x3_simt_kernel(const SimtAr
     if (a.act == kActRelu) {
       t = fmaxf(t, 0.f);
     } else if (a.act == kActSilu) {
-      const float s = r16(1.f / (1.f + expf(-t)));
+      const float s = r16(sigmoid_fast(t));
       t = r16(t * s);
     }
     if (a.add1) t = r16(t + __half2float(a.add1[obase + j]));
@@ -209,7 +209,7 @@ __global__ void __launch_bounds__(kSimtThreads) conv3x3_c1_kernel(const SimtArgs
     for (int j = 0; j < 8; ++j) {
       float t = r16(acc[j] + b[j]);
       if (a.act == kActRelu) t = fmaxf(t, 0.f);
-      else if (a.act == kActSilu) t = r16(t * r16(1.f / (1.f + expf(-t))));
+      else if (a.act == kActSilu) t = r16(t * r16(sigmoid_fast(t)));
       acc[j] = t;
     }
     const __half* adds[2] = {a.add1, a.add2};

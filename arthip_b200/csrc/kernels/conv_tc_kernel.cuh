@@ -163,12 +163,14 @@ __device__ __forceinline__ void hadd8v(uint32_t (&h)[4], const uint4& u) {
 template <int ACT>
 __device__ __forceinline__ void act8(uint32_t (&h)[4]) {
   if constexpr (ACT == kActSilu) {
+    // Sigmoid rounded to fp16, then the fp16 product: the fp32 product of two fp16 values
+    // is exact, so one rounded half2 multiply equals rounding it (the graph's Mul node).
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      const float2 t = __half22float2(*reinterpret_cast<__half2*>(&h[i]));
-      const float s0 = r16(1.f / (1.f + expf(-t.x)));
-      const float s1 = r16(1.f / (1.f + expf(-t.y)));
-      __half2 o = __floats2half2_rn(t.x * s0, t.y * s1);
+      const __half2 v = *reinterpret_cast<__half2*>(&h[i]);
+      const float2 t = __half22float2(v);
+      const __half2 sg = __floats2half2_rn(sigmoid_fast(t.x), sigmoid_fast(t.y));
+      __half2 o = __hmul2(v, sg);
       h[i] = *reinterpret_cast<uint32_t*>(&o);
     }
   } else if constexpr (ACT == kActRelu) {
@@ -184,7 +186,7 @@ __device__ __forceinline__ void act8(uint32_t (&h)[4]) {
 // Activation of one fp16-rounded conv output value (runtime selector).
 __device__ __forceinline__ float act1(float t, int act) {
   if (act == kActRelu) return fmaxf(t, 0.f);
-  if (act == kActSilu) return r16(t * r16(1.f / (1.f + expf(-t))));
+  if (act == kActSilu) return r16(t * r16(sigmoid_fast(t)));
   return t;
 }
 

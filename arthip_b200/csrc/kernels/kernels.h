@@ -17,6 +17,15 @@ namespace ah {
 
 enum Act : int { kActNone = 0, kActRelu = 1, kActSilu = 2 };
 
+#ifdef __CUDACC__
+// Logistic sigmoid for the SiLU epilogues and the Sigmoid op, from the hardware exp2 and
+// divide approximations (__expf, __fdividef: errors of a few fp32 ulp; 0 for very large
+// -v). Every caller rounds the result to fp16 next, which absorbs that error except where
+// the exact value lies within ~1e-6 of an fp16 rounding boundary (a one-ulp difference).
+// The libm expf and IEEE division made the SiLU convs epilogue-bound.
+__device__ __forceinline__ float sigmoid_fast(float v) { return __fdividef(1.f, 1.f + __expf(-v)); }
+#endif
+
 // ---------------------------------------------------------------------------
 // tcgen05 implicit-GEMM 3x3 convolution (conv_tc.cu)
 // ---------------------------------------------------------------------------

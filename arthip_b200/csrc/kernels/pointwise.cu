@@ -20,7 +20,7 @@ __global__ void unary_kernel(const __half* __restrict__ in, __half* __restrict__
   if (i >= n) return;
   const float x = __half2float(in[i]);
   float y;
-  if (op == kSigmoid) y = 1.f / (1.f + expf(-x));
+  if (op == kSigmoid) y = sigmoid_fast(x);
   else if (op == kRelu) y = fmaxf(x, 0.f);
   else y = fminf(fmaxf(x, lo), hi);
   out[i] = __float2half_rn(y);

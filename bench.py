@@ -60,6 +60,11 @@ CONFIG_TABLE = {
     "C4": ("R8F64", 4, 2160, 3840, "ArtCNN R8F64 fp16 fps @2160p per B200",
            "C4: ArtCNN-style R8F64 (18 conv3x3, ReLU, residual + global skip, DepthToSpace 2) fp16, 3840x2160 luma",
            TC_KERNEL),
+    # The shipped luma model's topology (27 convs: [conv+SiLU, conv+SiLU, conv + add] x 8,
+    # body conv + global skip, tail + DepthToSpace 2 + Clip) with random weights.
+    "ArtCNN": ("artcnn_silu", 2, 1080, 1920, "ArtCNN R8F64 (SiLU, shipped topology) fp16 fps @1080p per B200",
+               "ArtCNN R8F64 luma topology (27 conv3x3, SiLU, residual + global skip, DepthToSpace 2, Clip) fp16, "
+               "1920x1080, random weights", TC_KERNEL),
 }
 
 
@@ -175,7 +180,10 @@ def dist_barrier(world):
 
 def build_model(tmpdir: Path):
     from arthip_b200 import modelgen, onnx_proto as op
-    cm = modelgen.conv_chain(modelgen.CONFIGS[CFG], seed=SEED)
+    if CFG == "artcnn_silu":
+        cm = modelgen.artcnn_silu(seed=SEED)
+    else:
+        cm = modelgen.conv_chain(modelgen.CONFIGS[CFG], seed=SEED)
     p = tmpdir / f"{CFG}_seed{SEED}.onnx"
     op.save_model(cm.model, p)
     return cm, p
@@ -295,7 +303,8 @@ def main():
     ap.add_argument("--e2e-engines", type=int, default=2)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--config", default="C2", choices=sorted(CONFIG_TABLE),
-                    help="C2 (default): R8F64 1080p; C3: R16F96 1080p; C4: R8F64 2160p")
+                    help="C2 (default): R8F64 1080p; C3: R16F96 1080p; C4: R8F64 2160p; ArtCNN: the "
+                         "shipped SiLU topology at 1080p")
     ap.add_argument("--frame-split", action="store_true",
                     help="BASELINE config 4, second part: one 7680x4320 R8F64 frame split into row "
                          "strips across the ranks (strip latency, max over ranks)")
