@@ -418,6 +418,9 @@ cudaError_t conv_tc_launch(const ConvTcPlan& P, const __half* add1, const __half
   int variant = 4;
   if (P.out.mode == 0) {
     variant = act == kActRelu ? 1 : (act == kActSilu ? 2 : 0);
+    // SiLU over 64-channel slices: the epilogue math is the bound, so eight epilogue warps
+    // per pipe (one per lane quarter and channel group).
+    if (variant == 2 && P.vert && P.MT == 64) variant = 5;
   } else if (P.out.dts_b == 2 && (P.out.nchw || w->M == 4) && !a.add1 && P.n_msplit == 1 && w->M % 4 == 0 &&
              w->M <= 16 && w->M <= P.MT) {
     variant = 3;
@@ -431,7 +434,7 @@ cudaError_t conv_tc_launch(const ConvTcPlan& P, const __half* add1, const __half
   }();
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(P.grid_x, P.n_msplit);
-  cfg.blockDim = dim3(P.vert ? kThreads2 : kThreads);
+  cfg.blockDim = dim3(P.vert ? (variant == 5 ? kThreads2W : kThreads2) : kThreads);
   cfg.dynamicSmemBytes = P.smem_bytes;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];

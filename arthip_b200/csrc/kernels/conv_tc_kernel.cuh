@@ -60,7 +60,7 @@ constexpr int kSmemLimit = 232448;  // 227 KB opt-in dynamic shared memory per b
 constexpr int kStageTile = 2048;    // one 32-pixel x 32-channel fp16 staging tile
 constexpr int kTailBytes = 1024;    // barriers and flags
 constexpr int kSmemPerSm = 233472;  // shared memory of one SM (two CTAs share it)
-constexpr int kVariants = 5;        // EPI 0 x ACT {none, relu, silu}; EPI 1; EPI 2
+constexpr int kVariants = 6;        // EPI 0 x ACT {none, relu, silu}; EPI 1; EPI 2; SiLU wide
 
 struct ConvTcArgs {
   CUtensorMap maps[kTcMaxChunks];
@@ -106,7 +106,8 @@ typedef void (*KernelFn)(ConvTcArgs);
 
 // The instantiation for an input channel count (C % 16 == 0, 16 <= C <= 128), a
 // formulation (vertical window, or standard) and an output variant (0-2: NHWC with act
-// none/relu/silu, 3: 2x DepthToSpace tail, 4: general per-element output).
+// none/relu/silu, 3: 2x DepthToSpace tail, 4: general per-element output; vertical window
+// only: 5 = 2 with eight epilogue warps per pipe, 640 threads).
 KernelFn kernel_for(int C, bool vert, int variant);
 
 struct Segment {
@@ -633,10 +634,16 @@ __global__ void __launch_bounds__(kThreads, 1) conv3x3_tc_kernel(const __grid_co
 // epilogue of pipe 1 (warp w reads TMEM lane quarter w % 4 and all channel groups).
 // ---------------------------------------------------------------------------
 constexpr int kThreads2 = 384;
+// Wide epilogue (SiLU NHWC layers of 64 channels, whose epilogue math is the bound): eight
+// epilogue warps per pipe, one per (TMEM lane quarter, 32-channel group).
+constexpr int kThreads2W = 640;
+constexpr int kMaxEpiWarps2 = 16;
 
-template <int NC64, int NC32, int NC16, int EPI, int ACT>
-__global__ void __launch_bounds__(kThreads2, EPI == 1 ? 2 : 1) conv3x3_tc_vert2_kernel(const __grid_constant__ ConvTcArgs a) {
+template <int NC64, int NC32, int NC16, int EPI, int ACT, int WIDE>
+__global__ void __launch_bounds__(WIDE ? kThreads2W : kThreads2, EPI == 1 ? 2 : 1)
+    conv3x3_tc_vert2_kernel(const __grid_constant__ ConvTcArgs a) {
   using Cfg = ChunkCfg<NC64, NC32, NC16>;
+  static_assert(!WIDE || EPI == 0, "the wide epilogue is for NHWC outputs");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sW = smem;
@@ -651,8 +658,8 @@ __global__ void __launch_bounds__(kThreads2, EPI == 1 ? 2 : 1) conv3x3_tc_vert2_
   uint64_t* acce = accf + 2 * kMaxAcc;         // [2][kMaxAcc]
   uint64_t* wbar = acce + 2 * kMaxAcc;
   uint64_t* donebar = wbar + 1;                // [2]
-  uint64_t* rbar = donebar + 2;                // [kEpiWarps] residual tiles of the epilogue warps
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(rbar + kEpiWarps);
+  uint64_t* rbar = donebar + 2;                // [kMaxEpiWarps2] residual tiles of the epilogue warps
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(rbar + kMaxEpiWarps2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -674,12 +681,12 @@ __global__ void __launch_bounds__(kThreads2, EPI == 1 ? 2 : 1) conv3x3_tc_vert2_
     for (int i = 0; i < 2 * NACC; ++i) {
       const int pp = i / NACC, cc = i - pp * NACC;
       ptx::mbar_init(ptx::smem_u32(&accf[pp * kMaxAcc + cc]), 1);
-      ptx::mbar_init(ptx::smem_u32(&acce[pp * kMaxAcc + cc]), 4);
+      ptx::mbar_init(ptx::smem_u32(&acce[pp * kMaxAcc + cc]), WIDE ? 8 : 4);  // the pipe's epilogue warps
     }
     ptx::mbar_init(ptx::smem_u32(wbar), 1);
     ptx::mbar_init(ptx::smem_u32(&donebar[0]), 1);
     ptx::mbar_init(ptx::smem_u32(&donebar[1]), 1);
-    for (int i = 0; i < kEpiWarps; ++i) ptx::mbar_init(ptx::smem_u32(&rbar[i]), 1);
+    for (int i = 0; i < kMaxEpiWarps2; ++i) ptx::mbar_init(ptx::smem_u32(&rbar[i]), 1);
     *abort_flag = 0;
     ptx::fence_mbar_init();
   }
@@ -842,14 +849,17 @@ __global__ void __launch_bounds__(kThreads2, EPI == 1 ? 2 : 1) conv3x3_tc_vert2_
     }
     __syncwarp();
   } else {
-    // ---------------- epilogue (warps 4..11) ----------------
+    // ---------------- epilogue (warps 4..11; 4..19 when WIDE) ----------------
     ptx::griddep_wait();  // residual operands and the output buffer belong to earlier layers
-    const int pp = (warp - 4) >> 2;  // pipe
-    const int q = warp & 3;          // tensor-memory lane quarter this warp may access
     const int e = warp - 4;
+    const int pp = WIDE ? (e >> 3) : (e >> 2);    // pipe
+    const int q = warp & 3;                       // tensor-memory lane quarter this warp may access
+    constexpr int KG = WIDE ? 1 : 2;              // 32-channel groups of this warp
+    const int gsel = WIDE ? ((e >> 2) & 1) : 0;   // its first group
     const int ngroups = (a.MT + 31) / 32;
     const int act = ACT >= 0 ? ACT : a.act;
-    uint8_t* stage = sStage + e * a.stage_per_warp;
+    // (the same 32 KB of staging either way: 8 warps x 4 KB, or 16 x 2 KB)
+    uint8_t* stage = sStage + e * (WIDE ? kStageTile : a.stage_per_warp);
     uint64_t* paccf = accf + pp * kMaxAcc;
     uint64_t* pacce = acce + pp * kMaxAcc;
     const uint32_t tbase = tmem_base + pp * half_cols;
@@ -871,11 +881,12 @@ __global__ void __launch_bounds__(kThreads2, EPI == 1 ? 2 : 1) conv3x3_tc_vert2_
     bool res_inflight = false;
     auto issue_res = [&](int xw_, int yy) {  // lane 0
       uint32_t bytes = 0;
-      for (int g = 0; g < ngroups; ++g) bytes += min(32, a.MT - g * 32) * 64;
+      for (int k = 0; k < KG && gsel + k < ngroups; ++k) bytes += min(32, a.MT - (gsel + k) * 32) * 64;
       ptx::mbar_arrive_expect_tx(ptx::smem_u32(&rbar[e]), bytes);
-      for (int g = 0; g < ngroups; ++g) {
+      for (int k = 0; k < KG && gsel + k < ngroups; ++k) {
+        const int g = gsel + k;
         const CUtensorMap* map = min(32, a.MT - g * 32) == 32 ? &a.res_map32 : &a.res_map16;
-        ptx::tma_load_3d(ptx::smem_u32(stage + g * kStageTile), map, ptx::smem_u32(&rbar[e]), m0 + g * 32, xw_, yy);
+        ptx::tma_load_3d(ptx::smem_u32(stage + k * kStageTile), map, ptx::smem_u32(&rbar[e]), m0 + g * 32, xw_, yy);
       }
     };
     while (ok && it.next(sg)) {
@@ -903,7 +914,8 @@ __global__ void __launch_bounds__(kThreads2, EPI == 1 ? 2 : 1) conv3x3_tc_vert2_
             // operands are loaded into registers before the accumulator wait.
             if (y + 2 < sg.yb) {
 #pragma unroll
-              for (int g2 = 0; g2 < 2; ++g2) {
+              for (int k2 = 0; k2 < KG; ++k2) {
+                const int g2 = gsel + k2;
                 if (g2 >= ngroups) break;
                 const size_t off = (pix + 2 * static_cast<size_t>(a.W)) * a.M + m0 + g2 * 32;
                 if (lop1) ptx::prefetch_l2(lop1 + off);
@@ -911,15 +923,16 @@ __global__ void __launch_bounds__(kThreads2, EPI == 1 ? 2 : 1) conv3x3_tc_vert2_
               }
             }
 #pragma unroll
-            for (int g2 = 0; g2 < 2; ++g2) {
+            for (int k2 = 0; k2 < KG; ++k2) {
+              const int g2 = gsel + k2;
               if (g2 >= ngroups) break;
               const int cw = min(32, a.MT - g2 * 32);
               const size_t off = pix * a.M + m0 + g2 * 32;
 #pragma unroll
               for (int i = 0; i < 4; ++i) {
                 if (i * 8 >= cw) break;
-                if (lop1) pre[0][g2][i] = __ldg(reinterpret_cast<const uint4*>(lop1 + off + i * 8));
-                if (a.add2) pre[1][g2][i] = __ldg(reinterpret_cast<const uint4*>(a.add2 + off + i * 8));
+                if (lop1) pre[0][k2][i] = __ldg(reinterpret_cast<const uint4*>(lop1 + off + i * 8));
+                if (a.add2) pre[1][k2][i] = __ldg(reinterpret_cast<const uint4*>(a.add2 + off + i * 8));
               }
             }
           }
@@ -944,10 +957,11 @@ __global__ void __launch_bounds__(kThreads2, EPI == 1 ? 2 : 1) conv3x3_tc_vert2_
         // one chunk beyond the three-row window, so the MMA issuer waits on this release.
         uint32_t rrs[2][32];
 #pragma unroll
-        for (int k = 0; k < 2; ++k) {
-          if (k >= ngroups) break;
-          const uint32_t taddr = tbase + (static_cast<uint32_t>(q * 32) << 16) + acc * M + k * 32;
-          if (min(32, a.MT - k * 32) < 32) {
+        for (int k = 0; k < KG; ++k) {
+          const int g = gsel + k;
+          if (g >= ngroups) break;
+          const uint32_t taddr = tbase + (static_cast<uint32_t>(q * 32) << 16) + acc * M + g * 32;
+          if (min(32, a.MT - g * 32) < 32) {
             ptx::tmem_ld_32x32b_x16(taddr, rrs[k]);
           } else if (M & 31u) {  // 48-column chunks: 16-column loads at 16-aligned columns
             ptx::tmem_ld_32x32b_x16(taddr, rrs[k]);
@@ -970,8 +984,8 @@ __global__ void __launch_bounds__(kThreads2, EPI == 1 ? 2 : 1) conv3x3_tc_vert2_
           res_inflight = false;
         }
 #pragma unroll
-        for (int k = 0; k < 2; ++k) {
-          const int g = k;
+        for (int k = 0; k < KG; ++k) {
+          const int g = gsel + k;
           if (g >= ngroups) break;
           const int cw = min(32, a.MT - g * 32);
           const uint32_t (&rr)[32] = rrs[k];
@@ -1037,9 +1051,10 @@ __global__ void __launch_bounds__(kThreads2, EPI == 1 ? 2 : 1) conv3x3_tc_vert2_
           ptx::fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0 && xw < a.W) {
-            for (int g = 0; g < ngroups; ++g) {
+            for (int k = 0; k < KG && gsel + k < ngroups; ++k) {
+              const int g = gsel + k;
               const int cw = min(32, a.MT - g * 32);
-              const uint32_t src = ptx::smem_u32(stage + g * kStageTile);
+              const uint32_t src = ptx::smem_u32(stage + k * kStageTile);
               const CUtensorMap* map = cw == 32 ? &a.out_map32 : &a.out_map16;
               if (a.reduce_out) ptx::tma_reduce_add_3d(map, src, m0 + g * 32, xw, y);
               else ptx::tma_store_3d(map, src, m0 + g * 32, xw, y);
@@ -1085,11 +1100,12 @@ template <int NC64, int NC32, int NC16>
 KernelFn pick(bool vert, int variant) {
   if (vert) {
     switch (variant) {
-      case 0: return conv3x3_tc_vert2_kernel<NC64, NC32, NC16, 0, kActNone>;
-      case 1: return conv3x3_tc_vert2_kernel<NC64, NC32, NC16, 0, kActRelu>;
-      case 2: return conv3x3_tc_vert2_kernel<NC64, NC32, NC16, 0, kActSilu>;
-      case 3: return conv3x3_tc_vert2_kernel<NC64, NC32, NC16, 1, -1>;
-      default: return conv3x3_tc_vert2_kernel<NC64, NC32, NC16, 2, -1>;
+      case 0: return conv3x3_tc_vert2_kernel<NC64, NC32, NC16, 0, kActNone, 0>;
+      case 1: return conv3x3_tc_vert2_kernel<NC64, NC32, NC16, 0, kActRelu, 0>;
+      case 2: return conv3x3_tc_vert2_kernel<NC64, NC32, NC16, 0, kActSilu, 0>;
+      case 3: return conv3x3_tc_vert2_kernel<NC64, NC32, NC16, 1, -1, 0>;
+      case 4: return conv3x3_tc_vert2_kernel<NC64, NC32, NC16, 2, -1, 0>;
+      default: return conv3x3_tc_vert2_kernel<NC64, NC32, NC16, 0, kActSilu, 1>;
     }
   }
   switch (variant) {

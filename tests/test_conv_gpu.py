@@ -59,6 +59,7 @@ TC_CASES = [
     (96, 96, 7, 300, 0, 2),      # two slices, residual + global skip (first TMA-staged, second per lane)
     (32, 96, 9, 131, 2, 0),      # two slices from a 32-channel input, SiLU
     (64, 128, 10, 260, 0, 1),    # two 64-channel slices, staged residual
+    (64, 64, 19, 300, 2, 2),     # SiLU, 64 channels: eight epilogue warps per pipe, two residuals
     (64, 4, 13, 300, 1, 0),      # narrow tail over three strips, partial last strip
     (32, 3, 9, 253, 2, 1),       # narrow output with SiLU and a residual (per-element stores)
     (16, 1, 5, 127, 0, 0),       # one output channel, one pixel short of a strip
@@ -153,6 +154,7 @@ def test_timed_out_pipeline_wait_is_reported_and_recovers(monkeypatch):
 @pytest.mark.parametrize("C,M,H,W,act,nadds", [
     (64, 64, 37, 300, 1, 1),    # vertical window, block conv B
     (64, 64, 19, 131, 1, 2),    # block residual + global skip (only the last operand in place)
+    (64, 64, 13, 200, 2, 1),    # SiLU (eight epilogue warps per pipe), in place
     (32, 32, 9, 140, 1, 1),     # vertical window, 64B-swizzle chunk
     (96, 96, 13, 150, 1, 1),    # vertical window in two 48-channel slices
     (64, 128, 9, 140, 0, 2),    # two 64-channel slices, staged first operand, second in place
