@@ -144,3 +144,23 @@ def test_fresh_engines_agree(engine, tmp_path, device):
             first = out
         else:
             np.testing.assert_array_equal(out, first)
+
+
+def test_dead_residuals_are_added_in_place(tmp_path, device):
+    """Buffer assignment: a conv whose last residual operand dies at that conv writes over
+    it (the tensor-core kernel then adds it with reduce-add stores). In R8F64 that is block
+    convs B of blocks 2-8 and the global skip of block 8. Block 1's residual is the head
+    output, which the global skip still needs, so that conv writes a new buffer."""
+    from arthip_b200.engine import Engine
+    cm = modelgen.conv_chain(modelgen.CONFIGS["R8F64"], seed=2)
+    p = tmp_path / "r8f64.onnx"
+    op.save_model(cm.model, p)
+    eng = Engine(p, device=device)
+    eng.prepare(1, 64, 200)
+    labels = [o["label"] for o in eng.ops()]
+    adds = [lb for lb in labels if "+add" in lb]
+    assert len(adds) == 8
+    assert "in place" not in adds[0]
+    assert all("in place" in lb for lb in adds[1:]), adds
+    assert not any("in place" in lb for lb in labels if "+add" not in lb)
+    eng.close()
