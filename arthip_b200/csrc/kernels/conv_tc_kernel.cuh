@@ -631,7 +631,10 @@ __global__ void __launch_bounds__(kThreads, 1) conv3x3_tc_kernel(const __grid_co
 //
 // Warps: 0 and 3 = TMA producers (pipe 0 / 1; warp 0 also loads the weights), 1 and 2 =
 // MMA issuers (pipe 0 / 1; warp 1 allocates TMEM), 4..7 = epilogue of pipe 0 and 8..11 =
-// epilogue of pipe 1 (warp w reads TMEM lane quarter w % 4 and all channel groups).
+// epilogue of pipe 1 (warp w reads TMEM lane quarter w % 4 and all channel groups). With
+// WIDE (640 threads), 4..11 and 12..19 are the pipes' epilogues, warp w taking lane quarter
+// w % 4 and 32-channel group ((w - 4) / 4) % 2. The 2x DepthToSpace tail (EPI 1) is built
+// for two CTAs per SM, each with half of the TMEM columns.
 // ---------------------------------------------------------------------------
 constexpr int kThreads2 = 384;
 // Wide epilogue (SiLU NHWC layers of 64 channels, whose epilogue math is the bound): eight
