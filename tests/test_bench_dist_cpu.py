@@ -32,7 +32,9 @@ def _worker(rank: int, world: int, port: int, out_dir: str):
     m = bench.dist_max(1.5 + r, w)
     bench.dist_barrier(w)
     seeds = bench.frame_seeds(r, 8)
-    Path(out_dir, f"r{r}.json").write_text(json.dumps({"world": w, "max": m, "seeds": seeds}))
+    Path(out_dir, f"r{r}.json").write_text(json.dumps({"world": w, "max": m, "seeds": seeds,
+                                                        "nccl_log": [os.environ.get("NCCL_DEBUG"),
+                                                                     os.environ.get("NCCL_DEBUG_FILE")]}))
     dist.destroy_process_group()
 
 
@@ -44,6 +46,8 @@ def test_gloo_world2_max_and_disjoint_frame_shares(tmp_path):
     assert all(x["world"] == 2 for x in res)
     assert all(x["max"] == 2.5 for x in res)  # max over ranks, seen by every rank
     assert not set(res[0]["seeds"]) & set(res[1]["seeds"])
+    # stdout carries only the JSON line: NCCL's log (its version banner included) goes to stderr
+    assert all(x["nccl_log"] == ["WARN", "/dev/stderr"] for x in res)
 
 
 def test_reference_arm_prints_only_on_rank0():
