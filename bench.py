@@ -42,6 +42,22 @@ import numpy as np
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
+# The JSON result line goes to the process's original stdout; everything else written to
+# file descriptor 1 (library banners, e.g. NCCL's version line under torchrun) is sent to
+# stderr, so stdout carries exactly one line. Set up by `_claim_stdout` when run as a script.
+_RESULT_OUT = sys.stdout
+
+
+def _claim_stdout():
+    global _RESULT_OUT
+    sys.stdout.flush()
+    _RESULT_OUT = os.fdopen(os.dup(1), "w")
+    os.dup2(2, 1)
+
+
+def emit(line: dict):
+    print(json.dumps(line), file=_RESULT_OUT, flush=True)
+
 METRIC = "ArtCNN R8F64 fp16 fps @1080p per B200; box fps at 1/2/4/8 GPUs; % roofline"
 UNIT = "frames/s"
 H, W = 1080, 1920
@@ -225,7 +241,7 @@ def run_reference(args):
                        "(ONNX Runtime CPU is not installable on this image)"},
             "cpu_baseline": {"value": fps, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
             "e2e": {"value": fps, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
-    print(json.dumps(line))
+    emit(line)
     return 0
 
 
@@ -280,13 +296,13 @@ def run_frame_split(args):
         ms = dist_max(ev0.elapsed_time(ev1) / steps, world)
         dist_barrier(world)
     if rank == 0:
-        print(json.dumps({
+        emit({
             "metric": "R8F64 7680x4320 single-frame latency, row strips across GPUs", "value": ms, "unit": "ms",
             "n_gpus": world, "steps": steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": False,
             "scaling": "strong", "vs_baseline": None, "dtype": "fp16", "data": "synthetic",
             "config": {"workload": "C4 (second part): one 7680x4320 luma frame, R8F64",
                        "split": f"{world} row strips, {halo}-row recompute halo each side, no exchange",
-                       "strip_rows_rank0": st.rows}}))
+                       "strip_rows_rank0": st.rows}})
     if world > 1:
         import torch.distributed as dist
         dist.destroy_process_group()
@@ -493,7 +509,7 @@ def main():
                     "note": "per-op CUDA events in a pass right after the timed region; roofline uses it"},
         "cpu_baseline": cpu,
     }
-    print(json.dumps(line))
+    emit(line)
     if world > 1:
         import torch.distributed as dist
         dist.destroy_process_group()
@@ -501,4 +517,5 @@ def main():
 
 
 if __name__ == "__main__":
+    _claim_stdout()
     sys.exit(main())
