@@ -479,6 +479,10 @@ void ah_conv3x3_destroy(ah_conv* c) {
   delete c;
 }
 
+void ah_test_set_conv_fault_hook(int wait_limit_ms, int stall_row) {
+  ah::conv_tc_set_test_hook(wait_limit_ms, stall_row);
+}
+
 // ---------------------------------------------------------------------------
 // Host helpers
 // ---------------------------------------------------------------------------

@@ -15,13 +15,17 @@
 //  * the array holds kNoAllocWeightBytes of packed weights, which covers every layer the
 //    tensor-core kernel supports (C % 16 == 0, C <= 128, M <= 256); every GPU on which the
 //    library's device code is loaded holds the whole array until the process exits;
-//  * every call on a device shares the one array and leaves the last call's weights in it;
-//    the error word is cleared at the start of each call. Calls whose GPU work overlaps
-//    (other host threads, or other streams) race on the array and give wrong results:
-//    calls on a device are serialised on the host, and each call returns only after its
-//    kernel has finished;
-//  * the first call on a device looks up the array's device address (set-up); make that
-//    first call before any stream capture is started on that device.
+//  * every call on a device shares that device's array and leaves the last call's weights
+//    in it; the error word is cleared at the start of each call. Calls whose GPU work
+//    overlaps on one device (other host threads, or other streams) would race on the array
+//    and give wrong results, so calls on one device are serialised on the host and each
+//    call returns only after its kernel has finished. Calls on different devices run
+//    concurrently; they share only the host staging buffer, held while it is packed and
+//    copied;
+//  * each call looks up the array's device address (cudaGetSymbolAddress, which allocates
+//    nothing) with the device current, so a device reset between calls is harmless;
+//  * `stream` must belong to `device` (checked); the caller's current device is restored
+//    on return.
 #include <cuda_runtime.h>
 
 #include <cstring>
@@ -50,12 +54,13 @@ static __device__ __align__(256) uint8_t g_noalloc_scratch[ah::kNoAllocScratchBy
 namespace ah {
 namespace {
 
-// Host staging of the packed weights and bias (static storage: no heap either).
+// Host staging of the packed weights and bias (static storage: no heap either), shared by
+// all devices and guarded by g_host_mu while a call packs and copies it.
 alignas(64) uint8_t g_pack_host[kNoAllocWeightBytes];
 float g_bias_host[256];
 
-std::mutex g_mu;                                  // one call at a time, all devices
-uint8_t* g_scratch_dev[kNoAllocMaxDevices] = {};  // per-device address of the array
+std::mutex g_host_mu;                        // the staging arrays above
+std::mutex g_dev_mu[kNoAllocMaxDevices];     // one call at a time per device (its array)
 
 void copy_err(const std::string& s, char* dst, int len) {
   if (!dst || len <= 0) return;
@@ -65,17 +70,29 @@ void copy_err(const std::string& s, char* dst, int len) {
   dst[n] = '\0';
 }
 
-// Set-up, once per device, with that device current. Caller holds g_mu.
-cudaError_t scratch_base(int device, uint8_t** out) {
-  if (!g_scratch_dev[device]) {
-    void* p = nullptr;
-    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-    if (e != cudaSuccess) return e;
-    g_scratch_dev[device] = static_cast<uint8_t*>(p);
-  }
-  *out = g_scratch_dev[device];
+// Device address of the array on the current device. Called on every call, with the
+// call's device current.
+cudaError_t scratch_base(uint8_t** out) {
+  void* p = nullptr;
+  const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+  if (e != cudaSuccess) return e;
+  *out = static_cast<uint8_t*>(p);
   return cudaSuccess;
 }
+
+// Restores the caller's current device when the call returns.
+struct DeviceRestore {
+  int prev = -1;
+  DeviceRestore() {
+    if (cudaGetDevice(&prev) != cudaSuccess) {
+      prev = -1;
+      (void)cudaGetLastError();
+    }
+  }
+  ~DeviceRestore() {
+    if (prev >= 0) cudaSetDevice(prev);
+  }
+};
 
 }  // namespace
 
@@ -99,7 +116,8 @@ extern "C" int ah_conv3x3_run_noalloc(int device, int C, int M, const uint16_t* 
     copy_err("no-alloc conv: device index out of range", err, errlen);
     return 1;
   }
-  std::lock_guard<std::mutex> lock(g_mu);
+  DeviceRestore restore;
+  std::lock_guard<std::mutex> dev_lock(g_dev_mu[device]);
   cudaError_t e = cudaSetDevice(device);
   if (e != cudaSuccess) {
     copy_err(std::string("cudaSetDevice(") + std::to_string(device) + ") failed: " + cudaGetErrorString(e), err,
@@ -107,8 +125,19 @@ extern "C" int ah_conv3x3_run_noalloc(int device, int C, int M, const uint16_t* 
     (void)cudaGetLastError();
     return 1;
   }
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int sdev = device;
+  e = cudaStreamGetDevice(s, &sdev);
+  if (e != cudaSuccess || sdev != device) {
+    copy_err(e != cudaSuccess ? std::string("no-alloc conv: invalid stream: ") + cudaGetErrorString(e)
+                              : "no-alloc conv: the stream belongs to device " + std::to_string(sdev) +
+                                    ", not device " + std::to_string(device),
+             err, errlen);
+    (void)cudaGetLastError();
+    return 1;
+  }
   uint8_t* base = nullptr;
-  e = scratch_base(device, &base);
+  e = scratch_base(&base);
   if (e != cudaSuccess) {
     copy_err(std::string("cudaGetSymbolAddress of the no-alloc scratch failed: ") + cudaGetErrorString(e), err,
              errlen);
@@ -124,13 +153,10 @@ extern "C" int ah_conv3x3_run_noalloc(int device, int C, int M, const uint16_t* 
              err, errlen);
     return 1;
   }
-  conv_tc_pack_into(w_oihw_f16, L, g_pack_host);
-  for (int m = 0; m < L.Mpad; ++m) g_bias_host[m] = (bias && m < M) ? bias[m] : 0.f;
   L.wpack = base;
   L.bias = reinterpret_cast<float*>(base + kNoAllocBiasOff);
   uint32_t* status = reinterpret_cast<uint32_t*>(base + kNoAllocStatusOff);
 
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
   ConvTcOut to;
   to.ptr = out_nhwc;
   to.mode = (M % 16 == 0) ? 0 : 1;
@@ -143,11 +169,17 @@ extern "C" int ah_conv3x3_run_noalloc(int device, int C, int M, const uint16_t* 
     return 1;
   }
   // Stream-ordered: weights, bias and a cleared error word, then the kernel, then the word
-  // back. The host copies are pageable, so the staging arrays are free again on return of
-  // each copy call; the final synchronisation makes the call complete on return.
-  e = cudaMemcpyAsync(base, g_pack_host, bytes, cudaMemcpyHostToDevice, s);
-  if (e == cudaSuccess)
-    e = cudaMemcpyAsync(L.bias, g_bias_host, sizeof(float) * L.Mpad, cudaMemcpyHostToDevice, s);
+  // back. The host copies are from pageable memory, so each copy call returns once the
+  // staging arrays have been read (they are free for another device's call then); the final
+  // synchronisation makes the call complete on return.
+  {
+    std::lock_guard<std::mutex> host_lock(g_host_mu);
+    conv_tc_pack_into(w_oihw_f16, L, g_pack_host);
+    for (int m = 0; m < L.Mpad; ++m) g_bias_host[m] = (bias && m < M) ? bias[m] : 0.f;
+    e = cudaMemcpyAsync(base, g_pack_host, bytes, cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess)
+      e = cudaMemcpyAsync(L.bias, g_bias_host, sizeof(float) * L.Mpad, cudaMemcpyHostToDevice, s);
+  }
   if (e == cudaSuccess) e = cudaMemsetAsync(status, 0, sizeof(uint32_t), s);
   if (e == cudaSuccess)
     e = conv_tc_launch(plan, static_cast<const __half*>(add1), static_cast<const __half*>(add2), act, status, s);

@@ -5,6 +5,7 @@
 // conv_tc_c*.cu (one file per input-channel count) so they compile in parallel.
 
 #include <algorithm>
+#include <atomic>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
@@ -18,6 +19,10 @@ namespace ah {
 using namespace tck;
 
 namespace {
+
+// Failure-path test hook (ah_test_set_conv_fault_hook): 0 = off.
+std::atomic<int> g_test_wait_ms{0};
+std::atomic<int> g_test_stall_row{-1};
 
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
@@ -340,6 +345,12 @@ bool conv_tc_plan(const ConvTcWeights* w, const __half* in, int H, int W, const 
   return true;
 }
 
+void conv_tc_set_test_hook(int wait_limit_ms, int stall_row) {
+  const bool on = wait_limit_ms > 0 && wait_limit_ms <= 4000 && stall_row >= 0;
+  g_test_stall_row.store(on ? stall_row : -1, std::memory_order_relaxed);
+  g_test_wait_ms.store(on ? wait_limit_ms : 0, std::memory_order_relaxed);
+}
+
 cudaError_t conv_tc_launch(const ConvTcPlan& P, const __half* add1, const __half* add2, int act, uint32_t* status,
                            cudaStream_t stream) {
   const ConvTcWeights* w = P.w;
@@ -401,17 +412,13 @@ cudaError_t conv_tc_launch(const ConvTcPlan& P, const __half* add1, const __half
   a.nacc = P.nacc;
   a.acc_stride = P.acc_stride;
   a.tmem_cols = static_cast<uint32_t>(P.tmem_cols);
-  // Pipeline waits are bounded (4 s). Failure-path test hook, off unless both are set by a
-  // test: ARTHIP_WAIT_LIMIT_MS shortens the bound, ARTHIP_TEST_STALL_ROW makes every CTA
-  // arm that input row's slot without loading it, so the kernel must report a timed-out
-  // wait through the status word (and leave the context usable).
-  a.wait_limit_ns = 4000000000ull;
-  a.stall_row = -1;
-  if (const char* v = std::getenv("ARTHIP_WAIT_LIMIT_MS")) {
-    const long ms = std::strtol(v, nullptr, 10);
-    if (ms > 0 && ms <= 4000) a.wait_limit_ns = static_cast<unsigned long long>(ms) * 1000000ull;
-  }
-  if (const char* v = std::getenv("ARTHIP_TEST_STALL_ROW")) a.stall_row = static_cast<int>(std::strtol(v, nullptr, 10));
+  // Pipeline waits are bounded (4 s). The failure-path test hook (off unless a test sets
+  // it through ah_test_set_conv_fault_hook) shortens the bound and makes every CTA arm one
+  // input row's slot without loading it, so the kernel must report a timed-out wait
+  // through the status word and leave the context usable.
+  const int hook_ms = g_test_wait_ms.load(std::memory_order_relaxed);
+  a.wait_limit_ns = hook_ms > 0 ? static_cast<unsigned long long>(hook_ms) * 1000000ull : 4000000000ull;
+  a.stall_row = hook_ms > 0 ? g_test_stall_row.load(std::memory_order_relaxed) : -1;
   // Output variant: NHWC with a compile-time activation, the 2x DepthToSpace tail (every
   // conv channel in one CTA's first 32-channel group, no residual; NCHW output, which for
   // one output channel is also the NHWC layout), or general stores.

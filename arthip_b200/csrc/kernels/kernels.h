@@ -111,6 +111,10 @@ bool conv_tc_plan(const ConvTcWeights* w, const __half* in, int H, int W, const 
                   ConvTcPlan* plan, std::string* err);
 cudaError_t conv_tc_launch(const ConvTcPlan& plan, const __half* add1, const __half* add2, int act,
                            uint32_t* status, cudaStream_t stream);
+// Failure-path test hook for later launches (process-wide): wait bound in ms (1..4000) and
+// the CTA-relative input row whose slot every CTA arms without loading it. Any other value
+// turns it off (the default: 4 s bound, no stalled row).
+void conv_tc_set_test_hook(int wait_limit_ms, int stall_row);
 
 // ---------------------------------------------------------------------------
 // CUDA-core convolution for narrow layers (conv_simt.cu): C==1 heads, small M

@@ -49,6 +49,7 @@ SIGNATURES: dict[str, tuple] = {
     "ah_conv3x3_destroy": (None, [_vp]),
     "ah_conv3x3_run_noalloc": (_i32, [_i32, _i32, _i32, _vp, _vp, _i32, _vp, _i32, _i32, _vp, _vp, _vp, _vp,
                                       _cp, _i32]),
+    "ah_test_set_conv_fault_hook": (None, [_i32, _i32]),
     "ah_float_to_half_rne": (None, [_vp, _vp, _sz]),
     "ah_float_to_half_ftz": (None, [_vp, _vp, _sz]),
     "ah_half_to_float": (None, [_vp, _vp, _sz]),

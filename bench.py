@@ -17,12 +17,15 @@ e2e: the same metric through the public C ABI call ``ah_engine_run`` with pinned
   buffers: per step an H2D copy of the frame and a D2H copy of the 2x output; two engines
   on two host threads (``--e2e-engines``), as the reference's filter round-robins frames
   over engines, so one engine's copies overlap the other's kernels.
-roofline: the dominant kernel (the tcgen05 conv) as algorithmic direct-conv FLOPs per
-  launch / its mean duration, from a per-op pass right after the timed region that
-  launches the same ops with a CUDA event between consecutive ops (table on stderr).
---impl reference: the reference's CPU path (ONNX Runtime CPU is not installable here;
-  the oracle's torch-CPU restatement of the same graph) on all host cores, one 45-row
-  strip of the frame per step, at most ~100 s of CPU time in total.
+roofline: the dominant kernel, the block conv A (64->64 + bias + ReLU, 8 launches per
+  frame, ~43% of the frame): algorithmic direct-conv FLOPs per launch / its mean duration
+  from a per-op pass right after the timed region (the same ops with a CUDA event between
+  consecutive ops; table on stderr), against the burst bf16 peak; the memory-bound
+  residual convs are reported separately against HBM bandwidth ("memory_bound").
+cpu_baseline / --impl reference: the reference's CPU path (ONNX Runtime CPU is not
+  installable here; the oracle's torch-CPU restatement of the same graph) on all host
+  cores, timed over whole 1920x1080 frames: 3 in the cpu_baseline, one per step in the
+  reference arm.
 """
 
 from __future__ import annotations
@@ -182,6 +185,20 @@ def dist_max(v: float, world: int) -> float:
     return float(t.item())
 
 
+def dist_gather(obj, world: int) -> list:
+    """Every rank's `obj`, in rank order (all ranks call it)."""
+    if world == 1:
+        return [obj]
+    import torch.distributed as dist
+    out = [None] * world
+    dist.all_gather_object(out, obj)
+    return out
+
+
+def frames_local(steps: int, span_ms: float) -> float:
+    return steps / (span_ms / 1000.0) if span_ms > 0 else 0.0
+
+
 def frame_seeds(rank: int, n: int, base: int = SEED) -> list[int]:
     """Seeds of the synthetic frames rank `rank` processes: each rank works on its own
     share of the frame stream (weak scaling)."""
@@ -205,37 +222,58 @@ def build_model(tmpdir: Path):
     return cm, p
 
 
-def cpu_reference_fps(cm, rows: int, reps: int, threads: int, budget_s: float = 30.0):
-    """The oracle's torch-CPU restatement of the graph on a horizontal strip of the frame;
-    fps scales by 1080/rows (conv cost is linear in pixels). Stops after `reps` strips or
-    once `budget_s` seconds of strips have run, whichever comes first."""
+def _keep_freed_heap():
+    """glibc: serve large blocks from the heap and keep freed memory there, so the CPU path's
+    per-node 0.5 GB fp32 tensors are not mapped and page-faulted afresh on every node
+    (with the default mmap threshold that alone costs the torch-CPU frame several times)."""
+    try:
+        import ctypes
+        libc = ctypes.CDLL("libc.so.6")
+        libc.mallopt(-4, 0)          # M_MMAP_MAX: no mmap-backed blocks
+        libc.mallopt(-1, -1)         # M_TRIM_THRESHOLD -1: never return freed heap memory
+    except Exception:
+        pass
+
+
+def cpu_reference_fps(cm, frames: int, threads: int, warmup: int = 1, budget_s: float = 150.0):
+    """The oracle's torch-CPU restatement of the graph on whole frames of the workload.
+
+    `warmup` untimed passes first: up to two over a whole frame (which also grow the heap
+    to its working size), the rest over a 64-row strip; then `frames` whole frames, each timed on
+    its own; stops early once `budget_s` seconds of frames have run (at least one frame).
+    Returns (frames/s, sample text, frames timed, total seconds)."""
     from arthip_b200 import modelgen
     from oracle import onnx_cpu
-    x = modelgen.synthetic_frame(SEED, 1, rows, W).astype(np.float64)
-    onnx_cpu.run_model(cm.model, x[:, :, : max(8, rows // 8)], mode="fp32_nodes", threads=threads)  # warm
+    _keep_freed_heap()
+    x = modelgen.synthetic_frame(SEED, 1, H, W).astype(np.float64)
+    for i in range(max(0, warmup)):
+        onnx_cpu.run_model(cm.model, x if i < 2 else x[:, :, :64], mode="fp32_nodes", threads=threads)
     times = []
     t_start = time.perf_counter()
-    while len(times) < reps and (not times or time.perf_counter() - t_start < budget_s):
+    while len(times) < frames and (not times or time.perf_counter() - t_start < budget_s):
         t0 = time.perf_counter()
         onnx_cpu.run_model(cm.model, x, mode="fp32_nodes", threads=threads)
         times.append(time.perf_counter() - t0)
-    per_frame = statistics.median(times) * (H / rows)
-    return 1.0 / per_frame, (f"{rows}x{W} strip of the 1080p frame x{len(times)} (median), scaled by {H}/{rows}; "
-                             f"{threads} torch threads")
+    total = sum(times)
+    fps = len(times) / total
+    sample = (f"{len(times)} whole {W}x{H} frames ({', '.join(f'{t:.2f}' for t in times)} s), after "
+              f"{warmup} warm-up passes (up to two whole frames, the rest 64-row strips); {threads} torch threads")
+    return fps, sample, len(times), total
 
 
 def run_reference(args):
-    world, rank, _ = int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0")), 0
+    world, rank = int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
     import tempfile
     threads = os.cpu_count() or 1
     with tempfile.TemporaryDirectory() as td:
         cm, _ = build_model(Path(td))
-        rows = 45
-        fps, sample = cpu_reference_fps(cm, rows, max(1, args.steps), threads, budget_s=100.0)
+        # One whole frame per step, K steps; capped at 40 frames / 150 s so that a run with
+        # a large K still ends within a few minutes ("steps" reports the frames timed).
+        fps, sample, n, total = cpu_reference_fps(cm, min(max(1, args.steps), 40), threads, warmup=args.warmup)
     line = {"impl": "reference", "metric": METRIC, "value": fps, "unit": UNIT, "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 / fps, "higher_is_better": True,
+            "steps": n, "warmup": args.warmup, "ms_per_step": 1000.0 * total / n, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
             "config": {"workload": WORKLOAD, "host_path": "torch-CPU restatement of the ONNX graph "
                        "(ONNX Runtime CPU is not installable on this image)"},
@@ -412,7 +450,8 @@ def main():
         # round-robins frames over engines the same way, `num_streams`): each call of the
         # synchronous ah_engine_run copies its frame in, runs it and copies the result out,
         # and the threads overlap one engine's copies with another's kernels.
-        e2e_steps = args.e2e_steps or max(10, min(args.steps, 200))
+        # At least 200 frames whatever --steps is: a shorter e2e run is not steady.
+        e2e_steps = args.e2e_steps or 200
         n_eng = max(1, args.e2e_engines)
         engines = [eng] + [Engine(path, device=local) for _ in range(n_eng - 1)]
         hin = [[torch.from_numpy(modelgen.synthetic_frame(SEED + 7 + 4 * e + i, 1, H, W)).pin_memory()
@@ -433,8 +472,16 @@ def main():
             t.start()
         for t in workers:
             t.join()
-        e2e_s = dist_max(time.perf_counter() - t0, world)
+        e2e_local = time.perf_counter() - t0
+        e2e_s = dist_max(e2e_local, world)
         dist_barrier(world)
+        # Per-rank figures, so a multi-GPU line can name its limiter: device-resident fps
+        # against the rank's SM clock (power cap), e2e fps against its host copies.
+        per_rank = dist_gather({"rank": rank, "fps": frames_local(args.steps, ev0.elapsed_time(ev1)),
+                                "sm_mhz": clocks["sm_mhz"], "reasons": clocks["reasons"],
+                                "power_w_max": clocks.get("power_w_max"),
+                                "e2e_fps": e2e_steps / e2e_local,
+                                "e2e_copy_gbs": e2e_steps * (in_bytes + out_bytes) / e2e_local / 1e9}, world)
 
     if rank != 0:
         if world > 1:
@@ -443,13 +490,8 @@ def main():
         return 0
 
     fps = world * frames / (span_max / 1000.0)
-    # roofline of the dominant kernel: all tcgen05 conv launches of a frame
-    tc = [(o, t) for o, t in zip(ops, op_ms) if o["kind"] == "conv_tc"]
-    tc_flops = sum(o["flops"] for o, _ in tc)
-    tc_ms = sum(t for _, t in tc)
-    achieved_tflops = tc_flops / (tc_ms / 1e3) / 1e12 if tc_ms > 0 else 0.0
-    peak_tf = peaks.get("bf16_tflops_sustained", peaks.get("bf16_tflops"))
     frame_ms = span_max / frames
+    ridge = peaks["bf16_tflops"] * 1e12 / (peaks["hbm_gbs"] * 1e9)  # FLOP per byte
     roof = [max(o["flops"] / (peaks["bf16_tflops"] * 1e12), o["bytes"] / (peaks["hbm_gbs"] * 1e9)) * 1e3
             for o in ops]
     roof_ms = sum(roof)
@@ -461,15 +503,35 @@ def main():
               file=sys.stderr)
     print(f"sum of ops {sum(op_ms):.4f} ms/frame (events between ops); graph path {frame_ms:.4f} ms/frame",
           file=sys.stderr)
-    # DRAM bytes per tcgen05 conv launch from the committed one-pass ncu capture of this
-    # workload (ncu cannot run inside a timed bench).
+    # The dominant kernel: the group of identical tensor-core conv launches (same label, e.g.
+    # the 8 block convs A "64->64 relu") with the largest share of the frame. Its roofline
+    # is its algorithmic FLOPs per launch over its mean launch time, against the burst bf16
+    # peak (each launch is a ~0.1 ms kernel inside a short run).
+    groups: dict[str, list] = {}
+    for o, t in zip(ops, op_ms):
+        if o["kind"] == "conv_tc":
+            groups.setdefault(o["label"], []).append((o, t))
+    dom_label = max(groups, key=lambda k: sum(t for _, t in groups[k]))
+    dom = groups[dom_label]
+    dom_ms = sum(t for _, t in dom) / len(dom)
+    dom_flops, dom_bytes = dom[0][0]["flops"], dom[0][0]["bytes"]
+    dom_tensor = dom_flops / dom_bytes >= ridge
+    if dom_tensor:
+        achieved, peak, unit = dom_flops / (dom_ms / 1e3) / 1e12, peaks["bf16_tflops"], "TFLOP/s"
+    else:
+        achieved, peak, unit = dom_bytes / (dom_ms / 1e3) / 1e9, peaks["hbm_gbs"], "GB/s"
+    # The memory-bound tensor-core convs (the residual block convs B, the tail): their
+    # algorithmic bytes over their summed time, against HBM bandwidth.
+    mem = [(o, t) for o, t in zip(ops, op_ms) if o["kind"] == "conv_tc" and o["flops"] / o["bytes"] < ridge]
+    mem_ms = sum(t for _, t in mem)
+    mem_gbs = sum(o["bytes"] for o, _ in mem) / (mem_ms / 1e3) / 1e9 if mem_ms > 0 else None
+    # DRAM bytes per launch of the dominant kernel, from the committed one-pass ncu capture
+    # of this workload (ncu cannot run inside a timed bench).
     traffic = None
     tp = ROOT / "profiles" / "conv3x3_tc_kernel_traffic.json"  # captured on C2
-    if args.config != "C2":
-        tp = ROOT / "profiles" / "no_capture_for_this_config"
-    if tp.exists():
+    if args.config == "C2" and tp.exists() and dom_label.endswith("relu"):
         try:
-            traffic = json.loads(tp.read_text()).get("dram_bytes_per_launch")
+            traffic = json.loads(tp.read_text())["per_launch_mb"]["block_conv_A_relu"] * 1e6
         except Exception:
             traffic = None
     share = {}
@@ -481,7 +543,7 @@ def main():
     if not args.no_cpu_baseline:
         try:
             threads = os.cpu_count() or 1
-            cfps, sample = cpu_reference_fps(cm, 45, 3, threads)
+            cfps, sample, _, _ = cpu_reference_fps(cm, 3, threads, warmup=2)
             cpu = {"value": cfps, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample}
         except Exception as exc:  # the baseline is reported, never fatal
             cpu = {"value": None, "unit": UNIT, "cores": os.cpu_count(), "kind": "port", "sample": f"failed: {exc}"}
@@ -498,16 +560,24 @@ def main():
         "e2e": {"value": world * e2e_steps / e2e_s, "unit": UNIT, "h2d_bytes_per_step": in_bytes,
                 "d2h_bytes_per_step": out_bytes,
                 "api": f"ah_engine_run (synchronous, pinned host buffers), {n_eng} engines on {n_eng} host threads"},
-        "roofline": {"bound": "tensor", "achieved": achieved_tflops, "peak": peak_tf, "unit": "TFLOP/s",
-                     "frac": achieved_tflops / peak_tf, "traffic": traffic,
-                     "kernel": TC_KERNEL, "launches_per_frame": len(tc),
-                     "peak_source": f"{peak_src} bf16_tflops_sustained",
+        "roofline": {"bound": "tensor" if dom_tensor else "hbm", "achieved": achieved, "peak": peak, "unit": unit,
+                     "frac": achieved / peak, "traffic": traffic,
+                     "kernel": f"{TC_KERNEL}: {dom_label}", "launches_per_frame": len(dom),
+                     "mean_launch_ms": dom_ms, "algorithmic_per_launch": {"flops": dom_flops, "bytes": dom_bytes},
+                     "peak_source": f"{peak_src} {'bf16_tflops' if dom_tensor else 'hbm_gbs'} (burst)",
+                     "frac_vs_sustained_peak": (achieved / peaks.get("bf16_tflops_sustained", peak))
+                     if dom_tensor else None,
                      "frame_roofline_frac": roof_ms / frame_ms, "frame_roofline_ms": roof_ms},
+        "memory_bound": {"convs": len(mem), "achieved_gbs": mem_gbs, "peak_gbs": peaks["hbm_gbs"],
+                         "frac": mem_gbs / peaks["hbm_gbs"] if mem_gbs else None,
+                         "note": "tensor-core convs below the ridge point (residual block convs, tail): "
+                                 "algorithmic bytes / summed time"},
         "kernel_share": {k: v / tot for k, v in share.items()},
         "gpu_launches": frames * len(ops),
         "op_pass": {"frames": op_count, "ms_per_frame": sum(op_ms),
                     "note": "per-op CUDA events in a pass right after the timed region; roofline uses it"},
         "cpu_baseline": cpu,
+        "per_rank": per_rank,
     }
     emit(line)
     if world > 1:

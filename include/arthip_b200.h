@@ -127,14 +127,24 @@ void ah_conv3x3_destroy(ah_conv* c);
  * on the tensor-core kernel only (C % 16 == 0, C <= 128, M <= 256; anything else is rejected
  * with return 1 and a message). Calls no cudaMalloc / cudaFree: the packed weights, bias
  * and error word live in a fixed 591,104-byte __device__ array that every GPU that loads the
- * library keeps until exit. All calls share that array, so calls are serialised on the host
- * and each returns after its kernel has finished (work overlapping on the GPU would race
- * on the array). The first call on a device looks up the array's address: make it before
- * any stream capture on that device. Returns 0, 1 (bad arguments / unsupported) or 2
- * (CUDA error or a timed-out pipeline wait). */
+ * library keeps until exit. All calls on a device share that device's array, so calls on one
+ * device are serialised on the host and each returns after its kernel has finished (work
+ * overlapping on the GPU would race on the array); calls on different devices may run
+ * concurrently. `stream` must belong to `device` (else return 1); the caller's current
+ * device is restored on return. Each call looks up the array's device address with
+ * cudaGetSymbolAddress, which allocates nothing; make the first call on a device before
+ * any stream capture on it. Returns 0, 1 (bad arguments / unsupported) or 2 (CUDA error or
+ * a timed-out pipeline wait). */
 int ah_conv3x3_run_noalloc(int device, int C, int M, const uint16_t* w_oihw_f16, const float* bias, int act,
                            const void* in_nhwc, int H, int W, const void* add1, const void* add2,
                            void* out_nhwc, void* stream, char* err, int errlen);
+
+/* Test-only failure-path hook (no counterpart in the reference). For tensor-core conv launches made after the call, in this process:
+ * every pipeline wait is bounded by wait_limit_ms (1..4000) instead of 4 s, and every CTA
+ * arms the slot of its input row `stall_row` (counted from the CTA's first row) without
+ * loading it, so the kernel must report a timed-out wait through its status word without
+ * faulting. Any other arguments (e.g. 0, -1) turn it off, which is the default. */
+void ah_test_set_conv_fault_hook(int wait_limit_ms, int stall_row);
 
 /* ------------------------------------------------------------------------------
  * Host fp16 conversions used at load time (no GPU).

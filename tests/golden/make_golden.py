@@ -45,7 +45,10 @@ def _load_reference(ref_root: Path):
 
 
 def main(argv):
-    ref_root = Path(argv[0]) if argv else Path("/root/reference")
+    if not argv:
+        print("usage: python tests/golden/make_golden.py <reference project root>")
+        return 2
+    ref_root = Path(argv[0])
     ref = _load_reference(ref_root)
     cases = {}
 
@@ -104,7 +107,8 @@ def main(argv):
         manifest[case] = {"fixture": d["fixture"], "shape": list(d["expected"].shape)}
     (HERE / "manifest.json").write_text(json.dumps(manifest, indent=1, sort_keys=True) + "\n")
     print(f"wrote {len(cases)} golden cases to {HERE}")
+    return 0
 
 
 if __name__ == "__main__":
-    main(sys.argv[1:])
+    sys.exit(main(sys.argv[1:]))

@@ -71,6 +71,19 @@ def assert_frame_parity(got: np.ndarray, ref: np.ndarray, label: str, tol: float
 ULP1 = 2.0 ** -10  # fp16 spacing just below 1.0
 
 
+def report_parity(label: str, d16: float, p16: float, d32: float, p32: float, bar: float) -> None:
+    """Prints the achieved parity of a frame test and, when ARTHIP_PARITY_LOG names a file,
+    appends it there as one tab-separated line (label, max-abs and [0,1] PSNR against the
+    typed fp16 graph, the same against fp32 between nodes, the max-abs bar applied)."""
+    import os
+    line = f"{label}\t{d16:.4g}\t{p16:.2f}\t{d32:.4g}\t{p32:.2f}\t{bar:.4g}"
+    print("PARITY " + line)
+    path = os.environ.get("ARTHIP_PARITY_LOG")
+    if path:
+        with open(path, "a") as f:
+            f.write(line + "\n")
+
+
 def _gap01(a: np.ndarray, b: np.ndarray) -> float:
     return float(np.abs(np.clip(a, 0, 1) - np.clip(b, 0, 1)).max())
 
@@ -98,8 +111,9 @@ def check_against_oracles(got: np.ndarray, ref16: np.ndarray, ref32: np.ndarray,
     gap, rgap = _gap01(ref16, ref32), _relgap(ref32, ref16)
     print(f"{label}: engine vs fp16_nodes {_gap01(got, ref16):.4g} (oracle spread {spread:.4g}, bar {tol16:.4g}); "
           f"vs fp32_nodes {_gap01(got, ref32):.4g} (oracle gap {gap:.4g})")
-    assert_frame_parity(got, ref16, f"{label} vs oracle fp16_nodes", tol16, rel16)
-    assert_frame_parity(got, ref32, f"{label} vs oracle fp32_nodes", tol16 + gap, rel16 + rgap)
+    d16, p16 = assert_frame_parity(got, ref16, f"{label} vs oracle fp16_nodes", tol16, rel16)
+    d32, p32 = assert_frame_parity(got, ref32, f"{label} vs oracle fp32_nodes", tol16 + gap, rel16 + rgap)
+    report_parity(f"{label} (oracle spread {spread:.3g})", d16, p16, d32, p32, tol16)
 
 
 def torch_conv_layer(x_nhwc, w_oihw, bias, act, adds):

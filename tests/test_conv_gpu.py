@@ -123,12 +123,13 @@ def test_repeated_launches_are_bit_identical():
         assert torch.equal(o, outs[0])
 
 
-def test_timed_out_pipeline_wait_is_reported_and_recovers(monkeypatch):
+def test_timed_out_pipeline_wait_is_reported_and_recovers():
     """Failure detection without a GPU fault: every CTA arms one input row's slot without
     loading it, so the MMA issuer's bounded wait (shortened to 50 ms) runs out; the kernel
     must drain, free its tensor memory and report the timeout in the status word, and the
     same layer must then run correctly."""
     from arthip_b200.engine import Conv3x3
+    from arthip_b200.native import lib
     H, W, C, M = 37, 300, 64, 64
     g = torch.Generator(device="cpu").manual_seed(5)
     dev = torch.device("cuda:0")
@@ -138,12 +139,12 @@ def test_timed_out_pipeline_wait_is_reported_and_recovers(monkeypatch):
     out = torch.zeros(1, H, W, M, dtype=torch.float16, device=dev)
     conv = Conv3x3(w, b.astype(np.float32), act=1)
     s = torch.cuda.current_stream().cuda_stream
-    monkeypatch.setenv("ARTHIP_WAIT_LIMIT_MS", "50")
-    monkeypatch.setenv("ARTHIP_TEST_STALL_ROW", "1")  # every CTA reads >= 3 input rows
-    conv.run(x.data_ptr(), H, W, out.data_ptr(), stream=s)
-    assert conv.status() != 0, "a wait that cannot complete must be reported"
-    monkeypatch.delenv("ARTHIP_TEST_STALL_ROW")
-    monkeypatch.delenv("ARTHIP_WAIT_LIMIT_MS")
+    lib().ah_test_set_conv_fault_hook(50, 1)  # every CTA reads >= 3 input rows
+    try:
+        conv.run(x.data_ptr(), H, W, out.data_ptr(), stream=s)
+        assert conv.status() != 0, "a wait that cannot complete must be reported"
+    finally:
+        lib().ah_test_set_conv_fault_hook(0, -1)
     conv.run(x.data_ptr(), H, W, out.data_ptr(), stream=s)
     torch.cuda.synchronize()
     assert conv.status() == 0

@@ -7,10 +7,15 @@ Mirrors the rejection and fusion checks of the reference suite
 
 from __future__ import annotations
 
+from pathlib import Path
+
 import pytest
 
 from arthip_b200 import modelgen, onnx_proto as op
 from arthip_b200.engine import EngineHarnessError, inspect_model
+
+# The reference's shipped models, committed as test data (tests/fixtures/README.md).
+FIXTURE_MODELS = Path(__file__).resolve().parent / "fixtures" / "models"
 
 REF_MODELS = {
     "luma": "ArtCNN_R8F64_fp16.onnx",
@@ -91,10 +96,10 @@ def test_conv_chain_fuses_to_one_op_per_conv(tmp_path, cfg):
 
 def test_shipped_luma_model_fusion(tmp_path):
     import os
-    ref = os.environ.get("ARTHIP_REF_MODELS", "/root/reference/tests/fixtures/models")
+    ref = os.environ.get("ARTHIP_REF_MODELS", str(FIXTURE_MODELS))
     path = os.path.join(ref, REF_MODELS["luma"])
     if not os.path.exists(path):
-        pytest.skip("shipped reference models not present on this host")
+        pytest.skip("shipped models not present")
     info = inspect_model(path)
     ops = [l for l in info["ops"] if not l.startswith(("input", "output"))]
     assert len(ops) == 27 and all(l.startswith("Conv") for l in ops)
@@ -104,10 +109,10 @@ def test_shipped_luma_model_fusion(tmp_path):
 
 def test_shipped_chroma_model_folds_fp32_casts(tmp_path):
     import os
-    ref = os.environ.get("ARTHIP_REF_MODELS", "/root/reference/tests/fixtures/models")
+    ref = os.environ.get("ARTHIP_REF_MODELS", str(FIXTURE_MODELS))
     path = os.path.join(ref, REF_MODELS["chroma"])
     if not os.path.exists(path):
-        pytest.skip("shipped reference models not present on this host")
+        pytest.skip("shipped models not present")
     info = inspect_model(path)
     assert info["in_fp32"] and info["out_fp32"]
     assert info["in_channels"] == 3 and info["out_channels"] == 2

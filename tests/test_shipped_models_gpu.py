@@ -1,11 +1,13 @@
 """The reference's shipped ArtCNN R8F64 models (luma fp16 2x, chroma 3->2 fp32 IO, dehalo
-3->3 fp32 IO) on its photo fixtures, engine against the oracle.
+3->3 fp32 IO) on its photo fixtures, engine against the oracle, on BASELINE's fixed bar:
+max-abs <= 4e-3 and PSNR >= 55 dB on the [0,1] output, against both the typed fp16 graph
+and the fp32-between-nodes execution (the bar is not widened here).
 
-The model and photo files belong to the reference project and are not part of this
-repository. The test runs when ARTHIP_SHIPPED_DIR names a directory laid out like the
-reference's `tests/fixtures/` (`models/ArtCNN_R8F64_*.onnx`, `images/test_*.png`), and is
-skipped otherwise. Inputs are photo crops: grayscale for the luma model, YCbCr for the
-three-channel models (full-range, scaled to [0, 1]).
+The models and photos are copies of the reference project's test fixtures, committed under
+`tests/fixtures/` (see the README there); ARTHIP_SHIPPED_DIR may name another directory
+with the same layout. Inputs are photo crops: grayscale for the luma model, YCbCr for the
+three-channel models (full-range, scaled to [0, 1]) as the reference's chroma tests feed
+them (tests/correctness/test_plugin.py:204,241-251).
 """
 
 from __future__ import annotations
@@ -18,15 +20,12 @@ import pytest
 
 from arthip_b200 import onnx_proto as op
 from arthip_b200.engine import Engine
-from gpu_util import check_against_oracles
+from gpu_util import MAX_ABS_TOL, assert_frame_parity, report_parity
 from oracle import onnx_cpu
 
 pytestmark = pytest.mark.gpu
 
-_DIR = os.environ.get("ARTHIP_SHIPPED_DIR")
-if not _DIR or not (Path(_DIR) / "models").is_dir():
-    pytest.skip("ARTHIP_SHIPPED_DIR does not name the shipped models and photos", allow_module_level=True)
-ROOT = Path(_DIR)
+ROOT = Path(os.environ.get("ARTHIP_SHIPPED_DIR") or Path(__file__).resolve().parent / "fixtures")
 
 MODELS = [
     # file, PIL mode of the input, channels kept, fp32 IO, output channels, scale
@@ -57,9 +56,9 @@ def test_shipped_model_on_photo_crop(fname, mode, cin, fp32_io, cout, scale):
     xd = x.astype(np.float64)
     ref16 = onnx_cpu.run_model(model, xd, mode="fp16_nodes")
     ref32 = onnx_cpu.run_model(model, xd, mode="fp32_nodes")
-    variants = [onnx_cpu.run_model(model, xd, mode="fp16_nodes", reverse_channels=True),
-                onnx_cpu.run_model(model, xd, mode="fp16_nodes", use_torch=False)]
-    check_against_oracles(got, ref16, ref32, variants, fname)
+    d16, p16 = assert_frame_parity(got, ref16, f"{fname} vs fp16_nodes", MAX_ABS_TOL)
+    d32, p32 = assert_frame_parity(got, ref32, f"{fname} vs fp32_nodes", MAX_ABS_TOL)
+    report_parity(f"shipped {fname}, 80x136 crop of test_256.png", d16, p16, d32, p32, MAX_ABS_TOL)
 
 
 def test_shipped_luma_model_on_full_hd_photo():
@@ -67,11 +66,13 @@ def test_shipped_luma_model_on_full_hd_photo():
     (cuDNN, TF32 off), as the reference upscales a 1080p frame."""
     path = ROOT / "models" / "ArtCNN_R8F64_fp16.onnx"
     model = op.load_model(path)
-    x = _photo("test_1920.png", "L", 0, 0, 1080, 1920).astype(np.float16)
+    x = _photo("test_1920_luma.png", "L", 0, 0, 1080, 1920).astype(np.float16)
     got = Engine(path).run(x).astype(np.float64)
     assert got.shape == (1, 1, 2160, 3840)
     xd = x.astype(np.float64)
     ref16 = onnx_cpu.run_model(model, xd, mode="fp16_nodes", device="cuda:0")
     ref32 = onnx_cpu.run_model(model, xd, mode="fp32_nodes", device="cuda:0")
-    alt = onnx_cpu.run_model(model, xd, mode="fp16_nodes", device="cuda:0", reverse_channels=True)
-    check_against_oracles(got, ref16, ref32, [alt], "shipped luma model, 1080p photo (GPU fp32 reference)")
+    d16, p16 = assert_frame_parity(got, ref16, "luma 1080p vs fp16_nodes", MAX_ABS_TOL)
+    d32, p32 = assert_frame_parity(got, ref32, "luma 1080p vs fp32_nodes", MAX_ABS_TOL)
+    report_parity("shipped ArtCNN_R8F64_fp16.onnx, 1920x1080 test_1920 luma (GPU fp32 oracle)", d16, p16, d32, p32,
+                  MAX_ABS_TOL)
