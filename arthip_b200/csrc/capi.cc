@@ -307,6 +307,24 @@ int ah_engine_synchronize(ah_engine* e, char* err, int errlen) {
   return 0;
 }
 
+int ah_engine_enqueue_ops(ah_engine* e, int begin, int end, char* err, int errlen) {
+  if (!e) return 1;
+  std::string msg;
+  if (!e->eng->EnqueueOps(begin, end, msg)) {
+    CopyOut(msg, err, errlen);
+    return 2;
+  }
+  return 0;
+}
+
+int ah_engine_op_output(ah_engine* e, int i, void** ptr, int* rows, size_t* row_bytes, int* boundary) {
+  if (!e || !ptr || !rows || !row_bytes || !boundary) return 1;
+  bool b = false;
+  if (!e->eng->OpOutput(i, ptr, rows, row_bytes, &b)) return 1;
+  *boundary = b ? 1 : 0;
+  return 0;
+}
+
 void* ah_engine_stream(ah_engine* e) { return e ? static_cast<void*>(e->eng->stream()) : nullptr; }
 
 int ah_engine_timing_start(ah_engine* e, int max_frames, char* err, int errlen) {

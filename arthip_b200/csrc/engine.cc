@@ -1038,6 +1038,82 @@ bool Engine::EnsureBuilt(const std::vector<int64_t>& s4, std::string& error) {
 // ---------------------------------------------------------------------------
 // Execution
 // ---------------------------------------------------------------------------
+cudaError_t Engine::LaunchOp(size_t i, cudaStream_t s) {
+  const DevOp& d = dev_ops_[i];
+  cudaError_t e = cudaSuccess;
+  const __half* in = d.in_boundary ? nullptr : static_cast<const __half*>(BufPtr(d.in_buf));
+  void* out = d.out_boundary ? out_boundary_ : BufPtr(d.out_buf);
+  switch (d.kind) {
+    case 0:
+      e = conv_tc_launch(d.tc, static_cast<const __half*>(BufPtr(d.add_buf[0])),
+                         static_cast<const __half*>(BufPtr(d.add_buf[1])), d.act, status_, s);
+      break;
+    case 1: {
+      SimtOut so = d.sout;
+      so.ptr = out;
+      e = simt_conv_launch(conv_weights_[d.widx].sw, in, d.H, d.W, static_cast<const __half*>(BufPtr(d.add_buf[0])),
+                           static_cast<const __half*>(BufPtr(d.add_buf[1])), d.act, so, s);
+      break;
+    }
+    case 2:
+      e = unary_launch(in, static_cast<__half*>(out), d.numel, d.subop, d.lo, d.hi, s);
+      break;
+    case 3:
+      e = binary_launch(in, static_cast<const __half*>(BufPtr(d.in1_buf)), static_cast<__half*>(out), d.numel,
+                        d.subop, s);
+      break;
+    case 4: {
+      SimtOut so = d.sout;
+      so.ptr = out;
+      e = dts_launch(in, d.H, d.W, d.C, so, s);
+      break;
+    }
+    case 5:
+      e = nchw_to_nhwc_launch(in_boundary_, input_is_fp32_ ? 1 : 0, static_cast<__half*>(out), d.C, d.H, d.W, s);
+      break;
+    case 6:
+      e = nhwc_to_nchw_launch(in, out_boundary_, output_is_fp32_ ? 1 : 0, d.C, d.H, d.W, s);
+      break;
+  }
+  return e;
+}
+
+bool Engine::EnqueueOps(int begin, int end, std::string& error) {
+  std::lock_guard<std::mutex> lock(mutex_);
+  if (!built_) {
+    error = "engine is not prepared for a shape";
+    return false;
+  }
+  if (begin < 0 || end > static_cast<int>(dev_ops_.size()) || begin > end) {
+    error = "op range [" + std::to_string(begin) + ", " + std::to_string(end) + ") outside the plan's " +
+            std::to_string(dev_ops_.size()) + " ops";
+    return false;
+  }
+  if (!SetDevice(error)) return false;
+  for (int i = begin; i < end; ++i) {
+    const cudaError_t e = LaunchOp(static_cast<size_t>(i), stream_);
+    if (e != cudaSuccess) {
+      error = "kernel launch for op " + std::to_string(i) + " (" + dev_ops_[i].info.label + ") failed: " +
+              cudaGetErrorString(e);
+      (void)cudaGetLastError();
+      return false;
+    }
+  }
+  return true;
+}
+
+bool Engine::OpOutput(int i, void** ptr, int* rows, size_t* row_bytes, bool* boundary) const {
+  std::lock_guard<std::mutex> lock(mutex_);
+  if (!built_ || i < 0 || i >= static_cast<int>(dev_ops_.size())) return false;
+  const DevOp& d = dev_ops_[i];
+  *boundary = d.out_boundary;
+  *ptr = d.out_boundary ? out_boundary_ : BufPtr(d.out_buf);
+  const int ch = (d.kind == 0 || d.kind == 1) ? d.M : d.C;  // conv outputs M channels
+  *rows = d.H;
+  *row_bytes = static_cast<size_t>(d.W) * static_cast<size_t>(ch) * sizeof(__half);
+  return true;
+}
+
 bool Engine::LaunchFrame(bool with_events, std::string& error) {
   cudaStream_t s = stream_;
   auto ev = [&](size_t k) -> cudaError_t {
@@ -1052,41 +1128,7 @@ bool Engine::LaunchFrame(bool with_events, std::string& error) {
   }
   for (size_t i = 0; i < dev_ops_.size(); ++i) {
     const DevOp& d = dev_ops_[i];
-    cudaError_t e = cudaSuccess;
-    const __half* in = d.in_boundary ? nullptr : static_cast<const __half*>(BufPtr(d.in_buf));
-    void* out = d.out_boundary ? out_boundary_ : BufPtr(d.out_buf);
-    switch (d.kind) {
-      case 0:
-        e = conv_tc_launch(d.tc, static_cast<const __half*>(BufPtr(d.add_buf[0])),
-                           static_cast<const __half*>(BufPtr(d.add_buf[1])), d.act, status_, s);
-        break;
-      case 1: {
-        SimtOut so = d.sout;
-        so.ptr = out;
-        e = simt_conv_launch(conv_weights_[d.widx].sw, in, d.H, d.W, static_cast<const __half*>(BufPtr(d.add_buf[0])),
-                             static_cast<const __half*>(BufPtr(d.add_buf[1])), d.act, so, s);
-        break;
-      }
-      case 2:
-        e = unary_launch(in, static_cast<__half*>(out), d.numel, d.subop, d.lo, d.hi, s);
-        break;
-      case 3:
-        e = binary_launch(in, static_cast<const __half*>(BufPtr(d.in1_buf)), static_cast<__half*>(out), d.numel,
-                          d.subop, s);
-        break;
-      case 4: {
-        SimtOut so = d.sout;
-        so.ptr = out;
-        e = dts_launch(in, d.H, d.W, d.C, so, s);
-        break;
-      }
-      case 5:
-        e = nchw_to_nhwc_launch(in_boundary_, input_is_fp32_ ? 1 : 0, static_cast<__half*>(out), d.C, d.H, d.W, s);
-        break;
-      case 6:
-        e = nhwc_to_nchw_launch(in, out_boundary_, output_is_fp32_ ? 1 : 0, d.C, d.H, d.W, s);
-        break;
-    }
+    cudaError_t e = LaunchOp(i, s);
     if (e != cudaSuccess) {
       error = "kernel launch for op " + std::to_string(i) + " (" + d.info.label + ") failed: " + cudaGetErrorString(e);
       (void)cudaGetLastError();

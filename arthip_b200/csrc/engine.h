@@ -73,6 +73,14 @@ class Engine {
   bool Prepare(const std::vector<int64_t>& in_nchw, void** in_dev, void** out_dev, size_t* in_bytes,
                size_t* out_bytes, std::string& error);
   bool Enqueue(std::string& error);
+  // Launch ops [begin, end) of the prepared plan directly on the engine stream (no CUDA
+  // graph), so a caller can put its own work between ops (the per-layer halo exchange of
+  // a row-strip split).
+  bool EnqueueOps(int begin, int end, std::string& error);
+  // Output buffer of op i: device pointer, rows (the op's H) and bytes per row (W x
+  // channels fp16, NHWC), and whether it is the boundary output (NCHW, IO dtype: then
+  // rows / row_bytes describe the NHWC shape of the op, not the boundary layout).
+  bool OpOutput(int i, void** ptr, int* rows, size_t* row_bytes, bool* boundary) const;
   bool Synchronize(std::string& error);
   cudaStream_t stream() const { return stream_; }
 
@@ -127,6 +135,7 @@ class Engine {
   bool EnsureBuilt(const std::vector<int64_t>& in_nchw, std::string& error);
   bool UploadWeights(std::string& error);
   bool LaunchFrame(bool with_events, std::string& error);
+  cudaError_t LaunchOp(size_t i, cudaStream_t s);
   bool CheckStatus(std::string& error);
   void DestroyShapeState();
   void DestroyAll();

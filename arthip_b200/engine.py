@@ -222,6 +222,20 @@ class Engine:
         if self._lib.ah_engine_synchronize(self._h, err, _ERR_LEN) != 0:
             raise EngineHarnessError(_msg(err, "synchronize failed"))
 
+    def enqueue_ops(self, begin: int, end: int):
+        """Launch ops [begin, end) of the prepared plan on the engine stream (no graph)."""
+        err = _err()
+        if self._lib.ah_engine_enqueue_ops(self._h, begin, end, err, _ERR_LEN) != 0:
+            raise EngineHarnessError(_msg(err, "enqueue_ops failed"))
+
+    def op_output(self, i: int) -> tuple[int, int, int, bool]:
+        """Op i's output buffer: (device pointer, rows, bytes per row, is the boundary output)."""
+        ptr, rows, rb, bnd = ctypes.c_void_p(), ctypes.c_int(0), ctypes.c_size_t(0), ctypes.c_int(0)
+        if self._lib.ah_engine_op_output(self._h, i, ctypes.byref(ptr), ctypes.byref(rows), ctypes.byref(rb),
+                                         ctypes.byref(bnd)) != 0:
+            raise EngineHarnessError(f"no output for op {i}")
+        return ptr.value, rows.value, rb.value, bool(bnd.value)
+
     @property
     def stream(self) -> int:
         return self._lib.ah_engine_stream(self._h) or 0

@@ -35,6 +35,8 @@ SIGNATURES: dict[str, tuple] = {
                                  _cp, _i32]),
     "ah_engine_enqueue": (_i32, [_vp, _cp, _i32]),
     "ah_engine_synchronize": (_i32, [_vp, _cp, _i32]),
+    "ah_engine_enqueue_ops": (_i32, [_vp, _i32, _i32, _cp, _i32]),
+    "ah_engine_op_output": (_i32, [_vp, _i32, ctypes.POINTER(_vp), _i32p, _szp, _i32p]),
     "ah_engine_stream": (_vp, [_vp]),
     "ah_engine_timing_start": (_i32, [_vp, _i32, _cp, _i32]),
     "ah_engine_timing_read": (_i32, [_vp, _dp, _i32, _dp, _i32p, _cp, _i32]),

@@ -284,10 +284,15 @@ def run_reference(args):
 
 
 def run_frame_split(args):
-    """One 7680x4320 frame split into row strips, one per rank, each extended by the
-    model's receptive field (18 rows) so that no halo is exchanged between GPUs. Each rank
-    runs its strip device-resident through the captured CUDA graph; the frame latency is
-    the slowest rank's strip time (CUDA events, max over ranks)."""
+    """One 7680x4320 frame split into row strips, one per rank (second
+    part), in one of two forms:
+      * recompute: each rank's strip is extended by the model's receptive field (18 rows
+        for R8F64) on each side, so no halo is exchanged; the strip runs through the
+        captured CUDA graph;
+      * exchange: each rank runs its own rows plus one halo row per side, launching the
+        ops one at a time, and after each op swaps one row with each neighbour (NCCL
+        send/recv over NVLink, on the engine stream).
+    The frame latency is the slowest rank's strip time (CUDA events, max over ranks)."""
     import tempfile
 
     import torch
@@ -297,50 +302,67 @@ def run_frame_split(args):
         nbuild.build()
     from arthip_b200 import modelgen
     from arthip_b200.engine import Engine
-    from arthip_b200.strips import conv_depth, plan_strips
+    from arthip_b200.strips import (HaloStripRunner, conv_depth, exchange_dist, halo_window, plan_halo_strips,
+                                    plan_strips)
 
     H8, W8, seed = 4320, 7680, 4
     world, rank, local = dist_setup()
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
+    steps = max(1, min(args.steps, 20))
+    frame = modelgen.synthetic_frame(seed, 1, H8, W8)
     with tempfile.TemporaryDirectory() as td:
         cm, path = build_model(Path(td))
         eng = Engine(path, device=local)
-        halo = conv_depth(path)
-        st = plan_strips(H8, world, halo)[rank]
-        in_ptr, out_ptr, in_bytes, out_bytes = eng.prepare(1, st.rows, W8)
-        frame = modelgen.synthetic_frame(seed, 1, H8, W8)
-        window = torch.from_numpy(np.ascontiguousarray(frame[:, :, st.in_lo:st.in_hi, :]).reshape(-1)).to(dev)
         estream = torch.cuda.ExternalStream(eng.stream, device=dev)
+        halo = conv_depth(path)
+        if args.halo == "exchange":
+            st = plan_halo_strips(H8, world)[rank]
+            runner = HaloStripRunner(eng, st, W8, 1, dev)
+            runner.load_input(halo_window(frame, st))
+            strip_rows = st.local_rows
 
-        class _B:
-            __cuda_array_interface__ = {"shape": (in_bytes // 2,), "typestr": "<f2", "data": (in_ptr, False),
-                                        "version": 3}
-        dst = torch.as_tensor(_B(), device=dev)
-        steps = max(1, min(args.steps, 20))
-        with torch.cuda.stream(estream):
-            dst.copy_(window, non_blocking=True)
+            def one():
+                runner.run(lambda view: exchange_dist(view, st))
+        else:
+            st = plan_strips(H8, world, halo)[rank]
+            in_ptr, out_ptr, in_bytes, out_bytes = eng.prepare(1, st.rows, W8)
+            window = torch.from_numpy(np.ascontiguousarray(frame[:, :, st.in_lo:st.in_hi, :]).reshape(-1)).to(dev)
+
+            class _B:
+                __cuda_array_interface__ = {"shape": (in_bytes // 2,), "typestr": "<f2", "data": (in_ptr, False),
+                                            "version": 3}
+            dst = torch.as_tensor(_B(), device=dev)
+            with torch.cuda.stream(estream):
+                dst.copy_(window, non_blocking=True)
+            strip_rows = st.rows
+
+            def one():
+                eng.enqueue()
         for _ in range(args.warmup):
-            eng.enqueue()
+            one()
         eng.synchronize()
+        torch.cuda.synchronize()
         dist_barrier(world)
         ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         ev0.record(estream)
         for _ in range(steps):
-            eng.enqueue()
+            one()
         ev1.record(estream)
         eng.synchronize()
         torch.cuda.synchronize()
         ms = dist_max(ev0.elapsed_time(ev1) / steps, world)
         dist_barrier(world)
     if rank == 0:
+        split = (f"{world} row strips, {halo}-row recompute halo each side, no exchange" if args.halo == "recompute"
+                 else f"{world} row strips, 1 halo row per side exchanged after each of the "
+                      f"{halo - 1} inner layers (NCCL send/recv)")
         emit({
             "metric": "R8F64 7680x4320 single-frame latency, row strips across GPUs", "value": ms, "unit": "ms",
             "n_gpus": world, "steps": steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": False,
             "scaling": "strong", "vs_baseline": None, "dtype": "fp16", "data": "synthetic",
-            "config": {"workload": "C4 (second part): one 7680x4320 luma frame, R8F64",
-                       "split": f"{world} row strips, {halo}-row recompute halo each side, no exchange",
-                       "strip_rows_rank0": st.rows}})
+            "config": {"workload": "C4 (second part): one 7680x4320 luma frame, R8F64", "split": split,
+                       "halo_mode": args.halo, "strip_rows_rank0": strip_rows}})
     if world > 1:
         import torch.distributed as dist
         dist.destroy_process_group()
@@ -362,6 +384,9 @@ def main():
     ap.add_argument("--frame-split", action="store_true",
                     help="BASELINE config 4, second part: one 7680x4320 R8F64 frame split into row "
                          "strips across the ranks (strip latency, max over ranks)")
+    ap.add_argument("--halo", default="recompute", choices=["recompute", "exchange"],
+                    help="--frame-split form: receptive-field halo recomputed per strip, or a 1-row "
+                         "halo exchanged with the neighbours after every layer")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     global CFG, SEED, H, W, METRIC, WORKLOAD, TC_KERNEL

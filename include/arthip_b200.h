@@ -76,6 +76,15 @@ int ah_engine_prepare(ah_engine* e, int N, int C, int H, int W, void** in_dev, v
  * Replays a CUDA graph captured per resolution. */
 int ah_engine_enqueue(ah_engine* e, char* err, int errlen);
 int ah_engine_synchronize(ah_engine* e, char* err, int errlen);
+/* Launch ops [begin, end) of the prepared plan directly on the engine stream, one kernel
+ * each, no CUDA graph; asynchronous. For callers that put their own work between ops: the
+ * per-layer 1-row halo exchange of a frame split into row strips across GPUs (the
+ * reference has no split and rejects tiling, src/vapoursynth/vs_hip.cpp:466-494). */
+int ah_engine_enqueue_ops(ah_engine* e, int begin, int end, char* err, int errlen);
+/* Output buffer of op i of the prepared plan: device pointer, rows and bytes per row of its
+ * NHWC fp16 layout (W x channels x 2), and boundary = 1 when it writes the model output
+ * buffer (NCHW, IO dtype) instead. Returns 1 for a bad index or an unprepared engine. */
+int ah_engine_op_output(ah_engine* e, int i, void** ptr, int* rows, size_t* row_bytes, int* boundary);
 /* The engine's CUDA stream (cudaStream_t) for ordering caller copies with frames. */
 void* ah_engine_stream(ah_engine* e);
 
