@@ -10,6 +10,7 @@
 
 #include "../../include/arthip_b200.h"
 #include "engine.h"
+#include "ep_partition.h"
 #include "fp16_host.h"
 #include "kernels/kernels.h"
 
@@ -46,6 +47,11 @@ bool LoadAndBuild(const char* path, int device, ah::Engine* eng, std::string* er
 
 struct ah_engine {
   std::unique_ptr<ah::Engine> eng;
+};
+
+struct ah_ep_capability {
+  ah::onnx::Model model;
+  std::vector<ah::ep::Region> regions;
 };
 
 struct ah_conv {
@@ -500,6 +506,127 @@ void ah_conv3x3_destroy(ah_conv* c) {
 void ah_test_set_conv_fault_hook(int wait_limit_ms, int stall_row) {
   ah::conv_tc_set_test_hook(wait_limit_ms, stall_row);
 }
+
+// ---------------------------------------------------------------------------
+// ONNX Runtime execution-provider partition rules
+// ---------------------------------------------------------------------------
+int ah_ep_device_usable(int device) {
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess || device < 0 || device >= n) {
+    (void)cudaGetLastError();
+    return 0;
+  }
+  cudaDeviceProp p;
+  if (cudaGetDeviceProperties(&p, device) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return 0;
+  }
+  return p.major == 10 ? 1 : 0;  // the kernels are built for sm_100a only
+}
+
+int ah_ep_node_supported(const void* model, size_t model_bytes, int node_index) {
+  ah::onnx::Model m;
+  std::string e;
+  if (!model || !ah::onnx::ParseModel(static_cast<const uint8_t*>(model), model_bytes, &m, &e)) return -1;
+  return ah::ep::IsNodeSupported(m.graph, node_index, ah::ep::InferElemTypes(m.graph)) ? 1 : 0;
+}
+
+int ah_ep_get_capability(const void* model, size_t model_bytes, int context_ok, ah_ep_capability** out, char* err,
+                         int errlen) {
+  if (!model || !out) {
+    CopyOut("invalid capability arguments", err, errlen);
+    return 1;
+  }
+  auto c = std::make_unique<ah_ep_capability>();
+  std::string e;
+  if (!ah::onnx::ParseModel(static_cast<const uint8_t*>(model), model_bytes, &c->model, &e)) {
+    CopyOut("HIP EP: " + (e.empty() ? std::string("malformed model") : e), err, errlen);
+    return 1;
+  }
+  c->regions = ah::ep::GetCapability(c->model, context_ok != 0);
+  *out = c.release();
+  return 0;
+}
+
+int ah_ep_region_count(const ah_ep_capability* c) { return c ? static_cast<int>(c->regions.size()) : -1; }
+
+static const ah::ep::Region* EpRegion(const ah_ep_capability* c, int i) {
+  if (!c || i < 0 || i >= static_cast<int>(c->regions.size())) return nullptr;
+  return &c->regions[i];
+}
+
+int ah_ep_region_nodes(const ah_ep_capability* c, int region, int* nodes, int cap) {
+  const auto* r = EpRegion(c, region);
+  if (!r) return -1;
+  for (int i = 0; i < static_cast<int>(r->nodes.size()) && nodes && i < cap; ++i) nodes[i] = r->nodes[i];
+  return static_cast<int>(r->nodes.size());
+}
+
+static const std::vector<std::string>* EpValues(const ah::ep::Region* r, int kind) {
+  if (!r) return nullptr;
+  if (kind == 0) return &r->activations;
+  if (kind == 1) return &r->constants;
+  if (kind == 2) return &r->outputs;
+  return nullptr;
+}
+
+int ah_ep_region_value_count(const ah_ep_capability* c, int region, int kind) {
+  const auto* v = EpValues(EpRegion(c, region), kind);
+  return v ? static_cast<int>(v->size()) : -1;
+}
+
+int ah_ep_region_value(const ah_ep_capability* c, int region, int kind, int j, char* buf, int len) {
+  const auto* v = EpValues(EpRegion(c, region), kind);
+  if (!v || j < 0 || j >= static_cast<int>(v->size())) return 1;
+  CopyOut((*v)[j], buf, len);
+  return 0;
+}
+
+int ah_ep_region_name(const ah_ep_capability* c, int region, char* buf, int len) {
+  const auto* r = EpRegion(c, region);
+  if (!r) return 1;
+  CopyOut(r->name, buf, len);
+  return 0;
+}
+
+int ah_ep_region_inspect(const ah_ep_capability* c, int region, char* buf, int len, char* err, int errlen) {
+  const auto* r = EpRegion(c, region);
+  if (!r) {
+    CopyOut("no such region", err, errlen);
+    return 1;
+  }
+  ah::Engine eng(0);
+  std::string e;
+  if (!eng.BuildHostOnly(ah::ep::RegionModel(c->model, *r), e)) {
+    CopyOut("HIP EP: " + e, err, errlen);
+    return 1;
+  }
+  CopyOut(eng.Describe(), buf, len);
+  return 0;
+}
+
+int ah_ep_compile_region(const ah_ep_capability* c, int region, int device, ah_engine** out, char* err, int errlen) {
+  const auto* r = EpRegion(c, region);
+  if (!r || !out) {
+    CopyOut("HIP EP: no such region", err, errlen);
+    return 1;
+  }
+  if (!ah_ep_device_usable(device)) {
+    CopyOut("HIP EP: device context is not initialized (device " + std::to_string(device) + ")", err, errlen);
+    return 1;
+  }
+  auto h = std::make_unique<ah_engine>();
+  h->eng = std::make_unique<ah::Engine>(device);
+  std::string e;
+  if (!h->eng->Build(ah::ep::RegionModel(c->model, *r), e)) {
+    CopyOut("HIP EP: " + e, err, errlen);
+    return 1;
+  }
+  *out = h.release();
+  return 0;
+}
+
+void ah_ep_capability_destroy(ah_ep_capability* c) { delete c; }
 
 // ---------------------------------------------------------------------------
 // Host helpers

@@ -146,22 +146,30 @@ def inspect_model(path) -> dict:
 class Engine:
     """One persistent native engine (the object a plugin keeps per stream)."""
 
-    def __init__(self, model, device: int = 0):
+    def __init__(self, model, device: int = 0, _handle=None):
         self._lib = lib()
         self._h = ctypes.c_void_p()
         err = _err()
-        if isinstance(model, (bytes, bytearray)):
-            buf = ctypes.create_string_buffer(bytes(model), len(model))
-            rc = self._lib.ah_engine_create_from_bytes(buf, len(model), device, ctypes.byref(self._h), err, _ERR_LEN)
+        if _handle is not None:
+            self._h = _handle  # an engine the native side created (e.g. an EP region compile)
         else:
-            rc = self._lib.ah_engine_create_from_file(str(model).encode(), device, ctypes.byref(self._h), err,
-                                                      _ERR_LEN)
-        if rc != 0:
-            raise EngineHarnessError(_msg(err, "engine creation failed"))
+            if isinstance(model, (bytes, bytearray)):
+                buf = ctypes.create_string_buffer(bytes(model), len(model))
+                rc = self._lib.ah_engine_create_from_bytes(buf, len(model), device, ctypes.byref(self._h), err,
+                                                           _ERR_LEN)
+            else:
+                rc = self._lib.ah_engine_create_from_file(str(model).encode(), device, ctypes.byref(self._h), err,
+                                                          _ERR_LEN)
+            if rc != 0:
+                raise EngineHarnessError(_msg(err, "engine creation failed"))
         i32 = ctypes.c_int
         a, b, c, d = i32(0), i32(0), i32(0), i32(0)
         self._lib.ah_engine_info(self._h, ctypes.byref(a), ctypes.byref(b), ctypes.byref(c), ctypes.byref(d))
         self.in_fp32, self.out_fp32, self.in_channels, self.out_channels = bool(a.value), bool(b.value), c.value, d.value
+
+    @classmethod
+    def from_handle(cls, handle) -> "Engine":
+        return cls(None, _handle=handle)
 
     def close(self):
         if self._h:

@@ -44,6 +44,17 @@ SIGNATURES: dict[str, tuple] = {
     "ah_engine_op_info": (_i32, [_vp, _i32, _cp, _i32, _cp, _i32, _dp, _dp]),
     "ah_engine_describe": (_i32, [_vp, _cp, _i32]),
     "ah_model_inspect": (_i32, [_cp, _cp, _i32, _i32p, _i32p, _i32p, _i32p, _cp, _i32]),
+    "ah_ep_device_usable": (_i32, [_i32]),
+    "ah_ep_node_supported": (_i32, [_vp, _sz, _i32]),
+    "ah_ep_get_capability": (_i32, [_vp, _sz, _i32, ctypes.POINTER(_vp), _cp, _i32]),
+    "ah_ep_region_count": (_i32, [_vp]),
+    "ah_ep_region_nodes": (_i32, [_vp, _i32, _i32p, _i32]),
+    "ah_ep_region_value_count": (_i32, [_vp, _i32, _i32]),
+    "ah_ep_region_value": (_i32, [_vp, _i32, _i32, _i32, _cp, _i32]),
+    "ah_ep_region_name": (_i32, [_vp, _i32, _cp, _i32]),
+    "ah_ep_region_inspect": (_i32, [_vp, _i32, _cp, _i32, _cp, _i32]),
+    "ah_ep_compile_region": (_i32, [_vp, _i32, _i32, ctypes.POINTER(_vp), _cp, _i32]),
+    "ah_ep_capability_destroy": (None, [_vp]),
     "ah_conv3x3_create": (_i32, [_i32, _i32, _i32, _vp, _vp, _i32, ctypes.POINTER(_vp), _cp, _i32]),
     "ah_conv3x3_run": (_i32, [_vp, _vp, _i32, _i32, _vp, _vp, _vp, _vp, _cp, _i32]),
     "ah_conv3x3_kind": (_i32, [_vp]),

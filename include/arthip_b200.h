@@ -105,6 +105,43 @@ int ah_model_inspect(const char* model_path, char* buf, int len, int* in_fp32, i
                      int* cout, char* err, int errlen);
 
 /* ------------------------------------------------------------------------------
+ * ONNX Runtime execution-provider partition rules (the provider "HIPExecutionProvider",
+ * src/onnxruntime-hip/hip_execution_provider.{h,cc}). The ORT-facing shim hands the
+ * serialized model to these calls and maps the results onto ComputeCapability /
+ * NodeComputeInfo; nothing here needs ORT headers. Nodes are identified by their position
+ * in graph.node (ONNX node order is topological).
+ * ---------------------------------------------------------------------------- */
+typedef struct ah_ep_capability ah_ep_capability;
+
+/* 1 when `device` exists and is an sm_100 GPU (the provider's context initializes),
+ * else 0. HipExecutionProvider's constructor context check (hip_execution_provider.cc:164-175). */
+int ah_ep_device_usable(int device);
+/* IsNodeSupported (hip_execution_provider.cc:22-161) for node `node_index`, plus Relu:
+ * 1 supported, 0 not, -1 malformed model. */
+int ah_ep_node_supported(const void* model, size_t model_bytes, int node_index);
+/* GetCapability (hip_execution_provider.cc:180-335): the maximal runs of supported nodes
+ * that have exactly one activation input and one output. context_ok = 0 claims nothing,
+ * as the reference does without a usable device. */
+int ah_ep_get_capability(const void* model, size_t model_bytes, int context_ok, ah_ep_capability** out, char* err,
+                         int errlen);
+int ah_ep_region_count(const ah_ep_capability* c);
+/* Node positions of region `region` (writes up to cap; returns the count, -1 bad index). */
+int ah_ep_region_nodes(const ah_ep_capability* c, int region, int* nodes, int cap);
+/* The region's MetaDef values: kind 0 = activation inputs, 1 = initializer inputs,
+ * 2 = outputs. Count, then the j-th name. */
+int ah_ep_region_value_count(const ah_ep_capability* c, int region, int kind);
+int ah_ep_region_value(const ah_ep_capability* c, int region, int kind, int j, char* buf, int len);
+/* MetaDef name "HipKernel_graph_<k>". */
+int ah_ep_region_name(const ah_ep_capability* c, int region, char* buf, int len);
+/* The fused op list the region compiles to, without a GPU (for inspection and tests). */
+int ah_ep_region_inspect(const ah_ep_capability* c, int region, char* buf, int len, char* err, int errlen);
+/* Compile (hip_execution_provider.cc:337-406): build an engine for the region on `device`;
+ * run it with ah_engine_run (host NCHW IO in the region's IO dtype). Errors are prefixed
+ * "HIP EP: ". */
+int ah_ep_compile_region(const ah_ep_capability* c, int region, int device, ah_engine** out, char* err, int errlen);
+void ah_ep_capability_destroy(ah_ep_capability* c);
+
+/* ------------------------------------------------------------------------------
  * Single fused conv layer (3x3, stride 1, pad 1) on device NHWC fp16 tensors:
  * out = [add2 +] [add1 +] act(conv(in, w) + bias). Replaces one winograd_conv /
  * direct_conv dispatch (src/common/hip_kernels.h:143-483) as the engine issues it.
