@@ -403,5 +403,123 @@ bool LoadModelFile(const std::string& path, Model* out, std::string* err) {
   return ParseModel(buf.data(), buf.size(), out, err);
 }
 
+// ---------------------------------------------------------------------------
+// Encoder (the same subset): used to hand a converted model back to a caller.
+// ---------------------------------------------------------------------------
+namespace {
+
+void PutVarint(std::string* o, uint64_t v) {
+  while (v >= 0x80) {
+    o->push_back(static_cast<char>((v & 0x7F) | 0x80));
+    v >>= 7;
+  }
+  o->push_back(static_cast<char>(v));
+}
+void PutKey(std::string* o, uint32_t f, uint32_t wt) { PutVarint(o, (static_cast<uint64_t>(f) << 3) | wt); }
+void PutInt(std::string* o, uint32_t f, int64_t v) {
+  PutKey(o, f, 0);
+  PutVarint(o, static_cast<uint64_t>(v));
+}
+void PutBytes(std::string* o, uint32_t f, const std::string& b) {
+  PutKey(o, f, 2);
+  PutVarint(o, b.size());
+  o->append(b);
+}
+template <typename T>
+void PutPackedVarints(std::string* o, uint32_t f, const std::vector<T>& v) {
+  if (v.empty()) return;
+  std::string b;
+  for (T x : v) PutVarint(&b, static_cast<uint64_t>(static_cast<int64_t>(x)));
+  PutBytes(o, f, b);
+}
+template <typename T>
+void PutPackedFixed(std::string* o, uint32_t f, const std::vector<T>& v) {
+  if (v.empty()) return;
+  PutBytes(o, f, std::string(reinterpret_cast<const char*>(v.data()), v.size() * sizeof(T)));
+}
+
+std::string EncTensor(const Tensor& t) {
+  std::string o;
+  PutPackedVarints(&o, 1, t.dims);
+  PutInt(&o, 2, t.data_type);
+  PutPackedFixed(&o, 4, t.float_data);
+  PutPackedVarints(&o, 5, t.int32_data);
+  PutPackedVarints(&o, 7, t.int64_data);
+  PutBytes(&o, 8, t.name);
+  if (t.has_raw) PutBytes(&o, 9, t.raw_data);
+  PutPackedFixed(&o, 10, t.double_data);
+  return o;
+}
+
+std::string EncAttr(const Attribute& a) {
+  std::string o;
+  PutBytes(&o, 1, a.name);
+  switch (a.type) {
+    case kAttrFloat: {
+      PutKey(&o, 2, 5);
+      uint32_t b;
+      std::memcpy(&b, &a.f, 4);
+      for (int k = 0; k < 4; ++k) o.push_back(static_cast<char>((b >> (8 * k)) & 0xFF));
+      break;
+    }
+    case kAttrInt: PutInt(&o, 3, a.i); break;
+    case kAttrString: PutBytes(&o, 4, a.s); break;
+    case kAttrFloats: PutPackedFixed(&o, 7, a.floats); break;
+    case kAttrInts: PutPackedVarints(&o, 8, a.ints); break;
+    default: break;
+  }
+  PutInt(&o, 20, a.type);
+  return o;
+}
+
+std::string EncNode(const Node& n) {
+  std::string o;
+  for (const auto& i : n.inputs) PutBytes(&o, 1, i);
+  for (const auto& i : n.outputs) PutBytes(&o, 2, i);
+  if (!n.name.empty()) PutBytes(&o, 3, n.name);
+  PutBytes(&o, 4, n.op_type);
+  for (const auto& a : n.attrs) PutBytes(&o, 5, EncAttr(a));
+  if (!n.domain.empty()) PutBytes(&o, 7, n.domain);
+  return o;
+}
+
+std::string EncValueInfo(const ValueInfo& v) {
+  std::string shape;
+  for (int64_t d : v.dims) {
+    std::string dim;
+    if (d >= 0) PutInt(&dim, 1, d);
+    else PutBytes(&dim, 2, "?");
+    PutBytes(&shape, 1, dim);
+  }
+  std::string tt;
+  PutInt(&tt, 1, v.elem_type);
+  PutBytes(&tt, 2, shape);
+  std::string type;
+  PutBytes(&type, 1, tt);
+  std::string o;
+  PutBytes(&o, 1, v.name);
+  PutBytes(&o, 2, type);
+  return o;
+}
+
+}  // namespace
+
+std::string EncodeModel(const Model& m) {
+  std::string g;
+  for (const auto& n : m.graph.nodes) PutBytes(&g, 1, EncNode(n));
+  PutBytes(&g, 2, "arthip_b200");
+  for (const auto& t : m.graph.initializers) PutBytes(&g, 5, EncTensor(t));
+  for (const auto& v : m.graph.inputs) PutBytes(&g, 11, EncValueInfo(v));
+  for (const auto& v : m.graph.outputs) PutBytes(&g, 12, EncValueInfo(v));
+  std::string o;
+  PutInt(&o, 1, m.ir_version ? m.ir_version : 8);
+  PutBytes(&o, 7, g);
+  std::string opset;
+  PutBytes(&opset, 1, "");
+  PutInt(&opset, 2, m.opset ? m.opset : 13);
+  PutBytes(&o, 8, opset);
+  return o;
+}
+
 }  // namespace onnx
 }  // namespace ah

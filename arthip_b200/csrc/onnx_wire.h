@@ -95,6 +95,9 @@ struct Model {
 // Returns false with a message on malformed input.
 bool ParseModel(const uint8_t* data, size_t size, Model* out, std::string* err);
 bool LoadModelFile(const std::string& path, Model* out, std::string* err);
+// Serializes the same subset (nodes, initializers, graph input/output value infos, the
+// default-domain opset); symbolic dims are written as dim_param "?".
+std::string EncodeModel(const Model& m);
 
 }  // namespace onnx
 }  // namespace ah

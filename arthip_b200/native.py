@@ -63,6 +63,13 @@ SIGNATURES: dict[str, tuple] = {
     "ah_conv3x3_run_noalloc": (_i32, [_i32, _i32, _i32, _vp, _vp, _i32, _vp, _i32, _i32, _vp, _vp, _vp, _vp,
                                       _cp, _i32]),
     "ah_test_set_conv_fault_hook": (None, [_i32, _i32]),
+    "ah_convert_float_to_float16": (_i32, [_vp, _sz, _i32, _cp, _i32, _i32, _vp, _sz, _szp, _cp, _i32]),
+    "ah_load_onnx": (_i32, [_vp, _sz, _cp, _i64, _i64, _vp, _sz, _szp, _cp, _i32]),
+    "ah_vs_model_create": (_i32, [_vp, _vp, _sz, _cp, _vp, ctypes.POINTER(_vp), _cp, _i32]),
+    "ah_vs_model_output": (_i32, [_vp, _vp, _i32p]),
+    "ah_vs_model_get_frame": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _i32, _cp, _i32]),
+    "ah_vs_model_destroy": (None, [_vp]),
+    "ah_device_properties": (_i32, [_i32, _cp, _i32, _i64p, _i64p, _i64p]),
     "ah_float_to_half_rne": (None, [_vp, _vp, _sz]),
     "ah_float_to_half_ftz": (None, [_vp, _vp, _sz]),
     "ah_half_to_float": (None, [_vp, _vp, _sz]),

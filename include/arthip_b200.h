@@ -193,6 +193,81 @@ int ah_conv3x3_run_noalloc(int device, int C, int M, const uint16_t* w_oihw_f16,
 void ah_test_set_conv_fault_hook(int wait_limit_ms, int stall_row);
 
 /* ------------------------------------------------------------------------------
+ * VapourSynth filter hip.Model and its loading path (src/vapoursynth/vs_hip.cpp,
+ * onnx_utils.cpp, convert_float_to_float16.cpp) as plain C: a plugin shim built against
+ * VapourSynth4.h registers "Model" and maps VSMap arguments and VSFrame planes onto these.
+ * Errors of the filter calls are prefixed "hip.Model: ".
+ * ---------------------------------------------------------------------------- */
+
+/* fp32 -> fp16 model conversion at load time (convert_float_to_float16.cpp:294-611):
+ * fp32 initializers to fp16 with the converter's flush-to-zero rounding
+ * (convert_float_to_float16.cpp:165-186), fp32 graph IO to fp16 unless cast_input /
+ * cast_output keep it fp32 behind inserted boundary Casts, op types in the comma-separated
+ * op_block_list (may be NULL) kept fp32 with Casts around them. Writes the serialized model
+ * to `out` (out == NULL: only *out_bytes, the size); returns 1 on a parse error or a short
+ * buffer. */
+int ah_convert_float_to_float16(const void* model, size_t model_bytes, int force_fp16_initializers,
+                                const char* op_block_list, int cast_input, int cast_output, void* out, size_t cap,
+                                size_t* out_bytes, char* err, int errlen);
+/* loadONNX (onnx_utils.cpp:29-128): the model from bytes (or, with model == NULL, from
+ * `path`), one rank-4 input and one rank-4 output required; fixes the input to [1, C,
+ * tile_h, tile_w] and the output batch to 1. Same output convention as above. */
+int ah_load_onnx(const void* model, size_t model_bytes, const char* path, int64_t tile_w, int64_t tile_h, void* out,
+                 size_t cap, size_t* out_bytes, char* err, int errlen);
+
+/* A clip or frame format, in VapourSynth's terms (VSColorFamily: 0 undefined, 1 gray,
+ * 2 RGB, 3 YUV; VSSampleType: 0 integer, 1 float). width / height are the luma plane's. */
+typedef struct {
+  int color_family;
+  int sample_type;
+  int bits_per_sample;
+  int subsampling_w, subsampling_h;
+  int num_planes;
+  int width, height;
+} ah_vs_format;
+
+/* hip.Model's optional arguments (vs_hip.cpp:626-633). overlap / tilesize: number of
+ * values given (0 = absent) and the values. fp16 defaults to 1 when fp16_set is 0.
+ * flexible_output_prop: NULL or "" when absent. */
+typedef struct {
+  int device_id;
+  int num_streams;
+  int fp16_set;
+  int64_t fp16;
+  int overlap_n;
+  int64_t overlap[2];
+  int tilesize_n;
+  int64_t tilesize[2];
+  const char* flexible_output_prop;
+} ah_vs_args;
+
+typedef struct ah_vs_model ah_vs_model;
+
+/* hipCreate (vs_hip.cpp:337-591): validates the clip (gray / YUV / RGB, 8/16-bit integer or
+ * fp16/fp32, no subsampling) and the tiling arguments, loads the model from bytes (or from
+ * network_path when model is NULL), converts it to fp16 when fp16 (boundary Casts kept for
+ * fp32 clips), builds num_streams engines on device_id and checks the clip's plane count
+ * against the model's input channels. */
+int ah_vs_model_create(const ah_vs_format* clip, const void* model, size_t model_bytes, const char* network_path,
+                       const ah_vs_args* args, ah_vs_model** out, char* err, int errlen);
+/* The output clip format (gray, or RGB for a 3-channel output without the flexible
+ * protocol; fp32, fp16 or 16-bit integer; the model's scale applied to width / height) and
+ * the number of output channels (the flexible protocol's num_planes). */
+int ah_vs_model_output(const ah_vs_model* m, ah_vs_format* out_format, int* num_output_channels);
+/* hipGetFrame (vs_hip.cpp:77-321): one frame. src_planes / src_strides: the frame's planes
+ * (bytes per row); the next engine of the pool (round-robin) runs it; output channel c is
+ * written to dst_planes[c] for c < n_dst_planes. Thread-safe; returns 0, 1 (format) or 2
+ * (run failure). */
+int ah_vs_model_get_frame(ah_vs_model* m, const ah_vs_format* frame_format, const void* const* src_planes,
+                          const ptrdiff_t* src_strides, void* const* dst_planes, const ptrdiff_t* dst_strides,
+                          int n_dst_planes, char* err, int errlen);
+void ah_vs_model_destroy(ah_vs_model* m);
+/* hip.DeviceProperties (vs_hip.cpp:602-614): name, PCI device id, SM clock (kHz), global
+ * memory (bytes). Returns 1 for a bad device. */
+int ah_device_properties(int device, char* name, int namelen, int64_t* pci_device_id, int64_t* clock_rate_khz,
+                         int64_t* global_memory);
+
+/* ------------------------------------------------------------------------------
  * Host fp16 conversions used at load time (no GPU).
  * RNE: hip_engine.cc:1190-1232 (FloatToHalfBitsRNE). FTZ: convert_float_to_float16.cpp:165-186.
  * ---------------------------------------------------------------------------- */
