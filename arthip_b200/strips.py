@@ -193,7 +193,7 @@ class HaloStripRunner:
     engine stream."""
 
     def __init__(self, engine, st: HaloStrip, width: int, channels: int, device):
-        self.engine, self.st, self.device = engine, st, device
+        self.engine, self.st, self.device, self.width = engine, st, device, width
         self.in_ptr, self.out_ptr, self.in_bytes, self.out_bytes = engine.prepare(channels, st.local_rows, width)
         self.n_ops = len(engine.ops())
         self.views = []
@@ -219,10 +219,8 @@ class HaloStripRunner:
 
     def own_output(self, scale: int) -> np.ndarray:
         """Host copy of the owned output rows (NCHW): local output rows [scale, scale * (rows + 1))."""
-        import torch
         dt = np.float32 if self.engine.out_fp32 else np.float16
-        c = self.engine.out_channels
-        full_rows = self.st.local_rows * scale
+        _, c, full_rows, full_w = self.engine.output_shape(self.engine.in_channels, self.st.local_rows, self.width)
         buf = device_rows_view(self.out_ptr, 1, self.out_bytes, self.device)[0].cpu().numpy().view(dt)
-        full = buf.reshape(1, c, full_rows, -1)
+        full = buf.reshape(1, c, full_rows, full_w)
         return full[:, :, scale:scale * (self.st.rows + 1), :].copy()
