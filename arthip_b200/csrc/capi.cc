@@ -58,8 +58,11 @@ struct ah_conv {
   int device = 0;
   int C = 0, M = 0, act = 0;
   bool tc = false;
+  bool wino = false;
   ah::ConvTcWeights tcw;
   ah::SimtConvWeights sw;
+  ah::WinoWeights ww;
+  ah::WinoPlan wplan;
   ah::ConvTcPlan plan;
   const void* plan_in = nullptr;
   const void* plan_out = nullptr;
@@ -313,6 +316,16 @@ int ah_engine_synchronize(ah_engine* e, char* err, int errlen) {
   return 0;
 }
 
+int ah_engine_set_conv_algo(ah_engine* e, int algo, char* err, int errlen) {
+  if (!e) return 1;
+  std::string msg;
+  if (!e->eng->SetConvAlgo(algo, msg)) {
+    CopyOut(msg, err, errlen);
+    return 1;
+  }
+  return 0;
+}
+
 int ah_engine_enqueue_ops(ah_engine* e, int begin, int end, char* err, int errlen) {
   if (!e) return 1;
   std::string msg;
@@ -443,6 +456,46 @@ int ah_conv3x3_create(int device, int C, int M, const uint16_t* w, const float* 
   return 0;
 }
 
+int ah_conv3x3_create_winograd(int device, int C, int M, const uint16_t* w, const float* bias, int act,
+                               ah_conv** out, char* err, int errlen) {
+  if (!out || !w || act < 0 || act > 2) {
+    CopyOut("invalid conv arguments", err, errlen);
+    return 1;
+  }
+  if (!ah::wino_supported(C, M)) {
+    CopyOut("Winograd conv supports C = 64, M = 64 (got C=" + std::to_string(C) + ", M=" + std::to_string(M) + ")",
+            err, errlen);
+    return 1;
+  }
+  cudaError_t ce = cudaSetDevice(device);
+  if (ce != cudaSuccess) {
+    CopyOut(std::string("cudaSetDevice(") + std::to_string(device) + ") failed: " + cudaGetErrorString(ce), err,
+            errlen);
+    (void)cudaGetLastError();
+    return 1;
+  }
+  auto c = std::make_unique<ah_conv>();
+  c->device = device;
+  c->C = C;
+  c->M = M;
+  c->act = act;
+  c->wino = true;
+  int sms = 0;
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) == cudaSuccess && sms > 0) c->num_sms = sms;
+  ce = ah::wino_upload(w, bias, C, M, &c->ww);
+  if (ce == cudaSuccess) ce = cudaMalloc(&c->status, sizeof(uint32_t));
+  if (ce == cudaSuccess) ce = cudaMemset(c->status, 0, sizeof(uint32_t));
+  if (ce != cudaSuccess) {
+    CopyOut(std::string("conv weight upload failed: ") + cudaGetErrorString(ce), err, errlen);
+    (void)cudaGetLastError();
+    ah::wino_free(&c->ww);
+    if (c->status) cudaFree(c->status);
+    return 1;
+  }
+  *out = c.release();
+  return 0;
+}
+
 int ah_conv3x3_run(ah_conv* c, const void* in, int H, int W, const void* add1, const void* add2, void* out,
                    void* stream, char* err, int errlen) {
   if (!c || !in || !out || H <= 0 || W <= 0) {
@@ -452,7 +505,22 @@ int ah_conv3x3_run(ah_conv* c, const void* in, int H, int W, const void* add1, c
   cudaSetDevice(c->device);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   cudaError_t e;
-  if (c->tc) {
+  if (c->wino) {
+    if (c->plan_in != in || c->plan_out != out || c->plan_H != H || c->plan_W != W) {
+      std::string perr;
+      if (!ah::wino_plan(&c->ww, static_cast<const __half*>(in), H, W, static_cast<__half*>(out), c->num_sms,
+                         &c->wplan, &perr)) {
+        CopyOut(perr, err, errlen);
+        return 1;
+      }
+      c->plan_in = in;
+      c->plan_out = out;
+      c->plan_H = H;
+      c->plan_W = W;
+    }
+    e = ah::wino_launch(c->wplan, static_cast<const __half*>(add1), static_cast<const __half*>(add2), c->act,
+                        c->status, s);
+  } else if (c->tc) {
     if (c->plan_in != in || c->plan_out != out || c->plan_H != H || c->plan_W != W) {
       std::string perr;
       ah::ConvTcOut to;
@@ -483,7 +551,7 @@ int ah_conv3x3_run(ah_conv* c, const void* in, int H, int W, const void* add1, c
   return 0;
 }
 
-int ah_conv3x3_kind(ah_conv* c) { return c ? (c->tc ? 0 : 1) : -1; }
+int ah_conv3x3_kind(ah_conv* c) { return c ? (c->wino ? 2 : (c->tc ? 0 : 1)) : -1; }
 
 int ah_conv3x3_status(ah_conv* c, uint32_t* status) {
   if (!c || !status) return 1;
@@ -499,6 +567,7 @@ void ah_conv3x3_destroy(ah_conv* c) {
   cudaSetDevice(c->device);
   ah::conv_tc_free(&c->tcw);
   ah::simt_conv_free(&c->sw);
+  ah::wino_free(&c->ww);
   if (c->status) cudaFree(c->status);
   delete c;
 }

@@ -148,6 +148,9 @@ Engine::Engine(int device_id) : device_id_(device_id) {
   poison_ = EnvOn("VSHIP_POISON");
   sync_each_ = EnvOn("VSHIP_SYNC_EACH");
   no_graph_ = EnvOn("ARTHIP_NO_GRAPH") || prof_ || poison_ || sync_each_;
+  // Conv algorithm for 64 -> 64 layers: "winograd" opts into the Winograd kernel (the
+  // reference's numerics); anything else keeps the direct implicit GEMM. Read once here.
+  if (const char* a = std::getenv("ARTHIP_CONV_ALGO")) conv_algo_ = std::string(a) == "winograd" ? 1 : 0;
 }
 
 Engine::~Engine() { DestroyAll(); }
@@ -710,16 +713,36 @@ void Engine::DestroyShapeState() {
 
 void Engine::DestroyAll() {
   DestroyShapeState();
-  for (auto& cw : conv_weights_) {
-    conv_tc_free(&cw.tcw);
-    simt_conv_free(&cw.sw);
-  }
-  conv_weights_.clear();
-  weights_uploaded_ = false;
+  FreeWeights();
   if (status_) cudaFree(status_);
   status_ = nullptr;
   if (stream_) cudaStreamDestroy(stream_);
   stream_ = nullptr;
+}
+
+void Engine::FreeWeights() {
+  for (auto& cw : conv_weights_) {
+    conv_tc_free(&cw.tcw);
+    simt_conv_free(&cw.sw);
+    wino_free(&cw.ww);
+  }
+  conv_weights_.clear();
+  weights_uploaded_ = false;
+}
+
+bool Engine::SetConvAlgo(int algo, std::string& error) {
+  std::lock_guard<std::mutex> lock(mutex_);
+  if (algo != 0 && algo != 1) {
+    error = "conv algorithm must be 0 (direct) or 1 (winograd)";
+    return false;
+  }
+  if (algo == conv_algo_) return true;
+  if (!SetDevice(error)) return false;
+  // Weights are packed per algorithm: drop the plan and the packed weights, rebuilt lazily.
+  DestroyShapeState();
+  FreeWeights();
+  conv_algo_ = algo;
+  return true;
 }
 
 bool Engine::UploadWeights(std::string& error) {
@@ -738,9 +761,15 @@ bool Engine::UploadWeights(std::string& error) {
       for (int m = 0; m < M; ++m) bias[m] = HalfToFloat(WeightHalf(bs, m));
     }
     ConvWeights cw;
+    // Winograd only where its output form applies: a plain NHWC activation (not a fused
+    // DepthToSpace / Clip tail).
+    // The direct form's weights are always packed: it also runs a Winograd-eligible conv
+    // whose output is the graph boundary (NCHW in the IO dtype).
+    cw.wino = conv_algo_ == 1 && wino_supported(C, M) && !op.fuse_dts && !op.fuse_clip;
     cw.tc = conv_tc_supported(C, M, nullptr);
     cudaError_t e = cw.tc ? conv_tc_upload(w16.data(), bias.data(), C, M, &cw.tcw)
                           : simt_conv_upload(w16.data(), bias.data(), C, M, &cw.sw);
+    if (e == cudaSuccess && cw.wino) e = wino_upload(w16.data(), bias.data(), C, M, &cw.ww);
     conv_weights_.push_back(cw);
     if (e != cudaSuccess) {
       error = std::string("cudaMalloc/cudaMemcpy of conv weights failed: ") + cudaGetErrorString(e);
@@ -947,7 +976,17 @@ bool Engine::EnsureBuilt(const std::vector<int64_t>& s4, std::string& error) {
           d.sout.nchw = 1;
           d.sout.fp32 = output_is_fp32_ ? 1 : 0;
         }
-        if (cw.tc) {
+        if (cw.wino && !direct_here) {
+          d.kind = 7;
+          d.info.kind = "conv_wino";
+          std::string perr;
+          if (!wino_plan(&cw.ww, static_cast<const __half*>(bufs_[d.in_buf]), d.H, d.W,
+                         static_cast<__half*>(bufs_[d.out_buf]), num_sms_, &d.wp, &perr)) {
+            error = "conv plan failed: " + perr;
+            DestroyShapeState();
+            return false;
+          }
+        } else if (cw.tc) {
           d.kind = 0;
           d.info.kind = "conv_tc";
           ConvTcOut to;
@@ -1074,6 +1113,10 @@ cudaError_t Engine::LaunchOp(size_t i, cudaStream_t s) {
     case 6:
       e = nhwc_to_nchw_launch(in, out_boundary_, output_is_fp32_ ? 1 : 0, d.C, d.H, d.W, s);
       break;
+    case 7:
+      e = wino_launch(d.wp, static_cast<const __half*>(BufPtr(d.add_buf[0])),
+                      static_cast<const __half*>(BufPtr(d.add_buf[1])), d.act, status_, s);
+      break;
   }
   return e;
 }
@@ -1108,7 +1151,7 @@ bool Engine::OpOutput(int i, void** ptr, int* rows, size_t* row_bytes, bool* bou
   const DevOp& d = dev_ops_[i];
   *boundary = d.out_boundary;
   *ptr = d.out_boundary ? out_boundary_ : BufPtr(d.out_buf);
-  const int ch = (d.kind == 0 || d.kind == 1) ? d.M : d.C;  // conv outputs M channels
+  const int ch = (d.kind == 0 || d.kind == 1 || d.kind == 7) ? d.M : d.C;  // conv outputs M channels
   *rows = d.H;
   *row_bytes = static_cast<size_t>(d.W) * static_cast<size_t>(ch) * sizeof(__half);
   return true;

@@ -83,6 +83,10 @@ class Engine {
   bool OpOutput(int i, void** ptr, int* rows, size_t* row_bytes, bool* boundary) const;
   bool Synchronize(std::string& error);
   cudaStream_t stream() const { return stream_; }
+  // Conv algorithm for 64 -> 64 layers: 0 = direct implicit GEMM (default, exact fp16
+  // products), 1 = Winograd F(2x2,3x3) with fp16 transformed operands (the reference's
+  // numerics). Also set by ARTHIP_CONV_ALGO=winograd at construction. Drops the current plan.
+  bool SetConvAlgo(int algo, std::string& error);
 
   // Per-op timing over many frames (CUDA events on the engine stream, no host sync per
   // frame): TimingStart reserves events for up to max_frames; Enqueue then launches ops
@@ -109,7 +113,7 @@ class Engine {
  private:
   struct DevOp {
     OpType type = OpType::Conv;
-    int kind = 0;  // 0 conv_tc, 1 conv_simt, 2 unary, 3 binary, 4 dts, 5 nchw->nhwc, 6 nhwc->nchw
+    int kind = 0;  // 0 conv_tc, 1 conv_simt, 2 unary, 3 binary, 4 dts, 5 nchw->nhwc, 6 nhwc->nchw, 7 conv_wino
     int in_buf = -1, in1_buf = -1, add_buf[2] = {-1, -1}, out_buf = -1;
     bool out_boundary = false;  // writes the boundary output buffer
     bool in_boundary = false;   // reads the boundary input buffer
@@ -117,6 +121,7 @@ class Engine {
     int act = kActNone;
     int widx = -1;  // conv weights index
     ConvTcPlan tc;
+    WinoPlan wp;
     SimtOut sout;
     size_t numel = 0;
     int subop = 0;
@@ -125,8 +130,10 @@ class Engine {
   };
   struct ConvWeights {
     bool tc = false;
+    bool wino = false;
     ConvTcWeights tcw;
     SimtConvWeights sw;
+    WinoWeights ww;
   };
 
   bool Parse(const onnx::Model& model, std::string& error);
@@ -134,6 +141,7 @@ class Engine {
                        std::unordered_map<std::string, std::vector<int64_t>>& shapes) const;
   bool EnsureBuilt(const std::vector<int64_t>& in_nchw, std::string& error);
   bool UploadWeights(std::string& error);
+  void FreeWeights();
   bool LaunchFrame(bool with_events, std::string& error);
   cudaError_t LaunchOp(size_t i, cudaStream_t s);
   bool CheckStatus(std::string& error);
@@ -145,6 +153,7 @@ class Engine {
   int device_id_ = 0;
   cudaStream_t stream_ = nullptr;
   bool device_ready_ = false;
+  int conv_algo_ = 0;
   int num_sms_ = 148;
 
   std::string input_name_, output_name_;

@@ -117,6 +117,33 @@ cudaError_t conv_tc_launch(const ConvTcPlan& plan, const __half* add1, const __h
 void conv_tc_set_test_hook(int wait_limit_ms, int stall_row);
 
 // ---------------------------------------------------------------------------
+// Winograd F(2x2,3x3) tensor-core convolution, 64 -> 64 channels (conv_wino.cu): fp16
+// transformed operands (the reference's numerics), opt-in through the engine's conv
+// algorithm. NHWC fp16 output with the fused activation and up to two residual adds.
+// ---------------------------------------------------------------------------
+struct WinoWeights {
+  void* upack = nullptr;   // device: U = G g G^T, [2 output halves][16 points][32 x 64] swizzled
+  float* bias = nullptr;   // device: 64 fp32
+};
+struct WinoPlan {
+  const WinoWeights* w = nullptr;
+  int H = 0, W = 0;
+  __half* out = nullptr;
+  int units_x = 0;
+  long long units = 0;
+  int grid_x = 0;
+  CUtensorMap in_map;
+};
+bool wino_supported(int C, int M);
+cudaError_t wino_upload(const uint16_t* w_oihw_f16, const float* bias_or_null, int C, int M, WinoWeights* out);
+void wino_free(WinoWeights* w);
+bool wino_plan(const WinoWeights* w, const __half* in, int H, int W, __half* out, int num_sms, WinoPlan* plan,
+               std::string* err);
+// out may be the last residual operand (in place): each element is read before it is written.
+cudaError_t wino_launch(const WinoPlan& plan, const __half* add1, const __half* add2, int act, uint32_t* status,
+                        cudaStream_t stream);
+
+// ---------------------------------------------------------------------------
 // CUDA-core convolution for narrow layers (conv_simt.cu): C==1 heads, small M
 // tails (with fused DepthToSpace / Clip / boundary layout), odd channel counts.
 // ---------------------------------------------------------------------------

@@ -230,6 +230,12 @@ class Engine:
         if self._lib.ah_engine_synchronize(self._h, err, _ERR_LEN) != 0:
             raise EngineHarnessError(_msg(err, "synchronize failed"))
 
+    def set_conv_algo(self, algo: str):
+        """"direct" (default) or "winograd" for the 64 -> 64 convs; drops the current plan."""
+        err = _err()
+        if self._lib.ah_engine_set_conv_algo(self._h, {"direct": 0, "winograd": 1}[algo], err, _ERR_LEN) != 0:
+            raise EngineHarnessError(_msg(err, "set_conv_algo failed"))
+
     def enqueue_ops(self, begin: int, end: int):
         """Launch ops [begin, end) of the prepared plan on the engine stream (no graph)."""
         err = _err()
@@ -281,24 +287,27 @@ class Engine:
 
 
 class Conv3x3:
-    """One fused 3x3 conv layer on device NHWC fp16 tensors (pointers as ints)."""
+    """One fused 3x3 conv layer on device NHWC fp16 tensors (pointers as ints).
+    ``algo="winograd"`` selects the Winograd F(2x2,3x3) kernel (64 -> 64 channels)."""
 
-    def __init__(self, weight_oihw: np.ndarray, bias: np.ndarray | None, act: int = 0, device: int = 0):
+    def __init__(self, weight_oihw: np.ndarray, bias: np.ndarray | None, act: int = 0, device: int = 0,
+                 algo: str = "direct"):
         self._lib = lib()
         w16 = np.ascontiguousarray(weight_oihw.astype(np.float16)).view(np.uint16)
         m, c = int(weight_oihw.shape[0]), int(weight_oihw.shape[1])
         b = None if bias is None else np.ascontiguousarray(bias.astype(np.float16).astype(np.float32))
         self._h = ctypes.c_void_p()
         err = _err()
-        rc = self._lib.ah_conv3x3_create(device, c, m, w16.ctypes.data, None if b is None else b.ctypes.data, act,
-                                         ctypes.byref(self._h), err, _ERR_LEN)
+        create = self._lib.ah_conv3x3_create_winograd if algo == "winograd" else self._lib.ah_conv3x3_create
+        rc = create(device, c, m, w16.ctypes.data, None if b is None else b.ctypes.data, act, ctypes.byref(self._h),
+                    err, _ERR_LEN)
         if rc != 0:
             raise EngineHarnessError(_msg(err, "conv create failed"))
         self.C, self.M = c, m
 
     @property
     def kind(self) -> str:
-        return "conv_tc" if self._lib.ah_conv3x3_kind(self._h) == 0 else "conv_simt"
+        return {0: "conv_tc", 1: "conv_simt", 2: "conv_wino"}[self._lib.ah_conv3x3_kind(self._h)]
 
     def run(self, in_ptr: int, h: int, w: int, out_ptr: int, add1: int = 0, add2: int = 0, stream: int = 0):
         err = _err()

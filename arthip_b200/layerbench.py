@@ -2,7 +2,7 @@
 by default), through the ``ah_conv3x3_*`` C ABI.
 
     python -m arthip_b200.layerbench [--C 64 --M 64 --H 1080 --W 1920 --act 1 --adds 0]
-                                     [--warmup 3 --iters 20]
+                                     [--warmup 3 --iters 20] [--algo direct|winograd]
 
 Prints one JSON line: mean launch time from CUDA events around `iters` back-to-back
 launches on the current stream, the algorithmic direct-conv FLOPs (2*9*C*M*H*W) and bytes
@@ -48,6 +48,8 @@ def main(argv=None) -> int:
     ap.add_argument("--in-place", action="store_true",
                     help="write over the last residual operand (reduce-add stores); the "
                          "operand then accumulates across launches, which does not change the timing")
+    ap.add_argument("--algo", default="direct", choices=["direct", "winograd"],
+                    help="conv kernel: the direct implicit GEMM, or Winograd F(2x2,3x3) (64 -> 64 only)")
     ap.add_argument("--model", choices=["C4F32", "R8F64", "R16F96"],
                     help="time whole frames of this BASELINE chain (luma, 2x) at --H x --W through the "
                          "engine's CUDA graph instead of one layer (a small-frame case for profilers)")
@@ -68,7 +70,7 @@ def main(argv=None) -> int:
     rng = np.random.default_rng(args.seed)
     w = (rng.standard_normal((M, C, 3, 3)) * (2.0 / (9 * C)) ** 0.5).astype(np.float16)
     b = (rng.standard_normal(M) * 0.01).astype(np.float16).astype(np.float32)
-    conv = Conv3x3(w, b, act=args.act)
+    conv = Conv3x3(w, b, act=args.act, algo=args.algo)
     s = torch.cuda.current_stream().cuda_stream
     ptrs = [a.data_ptr() for a in adds]
     if args.in_place:
@@ -121,6 +123,7 @@ def _model_frames(args) -> int:
         path = Path(td) / f"{args.model}.onnx"
         op.save_model(cm.model, path)
         eng = Engine(path)
+        eng.set_conv_algo(args.algo)
         in_ptr, _, in_bytes, _ = eng.prepare(1, H, W)
         dev = torch.device("cuda:0")
         frame = torch.from_numpy(modelgen.synthetic_frame(args.seed, 1, H, W).reshape(-1)).to(dev)
@@ -139,7 +142,7 @@ def _model_frames(args) -> int:
             eng.enqueue()
         eng.synchronize()
         ms = (time.perf_counter() - t0) * 1e3 / args.iters
-        print(json.dumps({"model": f"{args.model} {H}x{W}", "ms_per_frame": ms, "fps": 1e3 / ms,
+        print(json.dumps({"model": f"{args.model} {H}x{W}", "algo": args.algo, "ms_per_frame": ms, "fps": 1e3 / ms,
                           "iters": args.iters, "timing": "host wall clock around enqueued graph replays"}))
         eng.close()
     return 0

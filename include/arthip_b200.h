@@ -76,6 +76,13 @@ int ah_engine_prepare(ah_engine* e, int N, int C, int H, int W, void** in_dev, v
  * Replays a CUDA graph captured per resolution. */
 int ah_engine_enqueue(ah_engine* e, char* err, int errlen);
 int ah_engine_synchronize(ah_engine* e, char* err, int errlen);
+/* Conv algorithm of the engine's 64 -> 64 layers (no counterpart setting in the reference,
+ * which always runs Winograd): 0 = direct implicit GEMM on tcgen05 (default; exact fp16
+ * products), 1 = Winograd F(2x2,3x3) on tcgen05 with fp16 transformed operands, the
+ * reference's own numerics (accurate on trained models, outside a 4e-3 bar on deep
+ * random-weight chains). The environment variable ARTHIP_CONV_ALGO=winograd selects 1 at
+ * engine creation. Drops the current plan; returns 1 for another value. */
+int ah_engine_set_conv_algo(ah_engine* e, int algo, char* err, int errlen);
 /* Launch ops [begin, end) of the prepared plan directly on the engine stream, one kernel
  * each, no CUDA graph; asynchronous. For callers that put their own work between ops: the
  * per-layer 1-row halo exchange of a frame split into row strips across GPUs (the
@@ -159,7 +166,14 @@ int ah_conv3x3_create(int device, int C, int M, const uint16_t* w_oihw_f16, cons
  * bit for bit. It must not overlap in_nhwc. */
 int ah_conv3x3_run(ah_conv* c, const void* in_nhwc, int H, int W, const void* add1, const void* add2,
                    void* out_nhwc, void* stream, char* err, int errlen);
-/* 0 = tcgen05 tensor-core kernel, 1 = CUDA-core kernel. */
+/* The same layer on the Winograd F(2x2,3x3) tcgen05 kernel (C = 64, M = 64 only; else
+ * return 1): the reference's own algorithm and numerics (winograd_conv,
+ * src/common/hip_kernels.h:143-396, weights U = G g G^T rounded to fp16,
+ * src/vapoursynth/hip_engine.cc:972-1009). fp16 transformed operands make it less exact
+ * than the direct kernel; run with ah_conv3x3_run. */
+int ah_conv3x3_create_winograd(int device, int C, int M, const uint16_t* w_oihw_f16, const float* bias, int act,
+                               ah_conv** out, char* err, int errlen);
+/* 0 = tcgen05 direct implicit GEMM, 1 = CUDA-core kernel, 2 = tcgen05 Winograd. */
 int ah_conv3x3_kind(ah_conv* c);
 /* Reads and clears the device error word the tensor-core kernel writes on a timed-out
  * pipeline wait (0 = none). Synchronises the device. */
