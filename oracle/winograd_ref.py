@@ -87,3 +87,23 @@ def conv_layer(x_nhwc: torch.Tensor, w_oihw: np.ndarray, bias, act: int, adds) -
     for a in adds:
         y = (y + a.float()).half().float()
     return y.contiguous()
+
+
+def conv2d_nchw(x: torch.Tensor, w: torch.Tensor, b) -> torch.Tensor:
+    """Conv output before the node's fp16 rounding (Y + bias in fp32) with the Winograd
+    numerics, for an NCHW fp32 tensor holding fp16 values: the form the ONNX oracle's
+    executor takes for its Conv node (``onnx_cpu._Exec.conv``)."""
+    _, C, H, W = x.shape
+    M = w.shape[0]
+    th, tw = (H + 1) // 2, (W + 1) // 2
+    xp = F.pad(x.half(), (1, 2 * tw + 2 - W - 1, 1, 2 * th + 2 - H - 1))
+    v = _input_transform(xp.unfold(2, 4, 2).unfold(3, 4, 2)).float()[0]
+    u = torch.from_numpy(weight_transform(w.cpu().numpy().astype(np.float16))).to(x.device).float()
+    m = torch.einsum("mcpq,ctupq->mtupq", u, v)
+    sq = [m[..., 0] + m[..., 1] + m[..., 2], m[..., 1] - m[..., 2] - m[..., 3]]
+    y = torch.stack([torch.stack([s[..., 0] + s[..., 1] + s[..., 2], s[..., 1] - s[..., 2] - s[..., 3]], dim=-1)
+                     for s in sq], dim=-1)
+    y = y.permute(0, 1, 3, 2, 4).reshape(M, 2 * th, 2 * tw)[:, :H, :W][None]
+    if b is not None:
+        y = y + b.float().view(1, -1, 1, 1)
+    return y
