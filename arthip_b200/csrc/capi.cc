@@ -59,10 +59,13 @@ struct ah_conv {
   int C = 0, M = 0, act = 0;
   bool tc = false;
   bool wino = false;
+  bool pair = false;
   ah::ConvTcWeights tcw;
   ah::SimtConvWeights sw;
   ah::WinoWeights ww;
   ah::WinoPlan wplan;
+  ah::PairWeights pw;
+  ah::PairPlan pplan;
   ah::ConvTcPlan plan;
   const void* plan_in = nullptr;
   const void* plan_out = nullptr;
@@ -456,14 +459,17 @@ int ah_conv3x3_create(int device, int C, int M, const uint16_t* w, const float* 
   return 0;
 }
 
-int ah_conv3x3_create_winograd(int device, int C, int M, const uint16_t* w, const float* bias, int act,
-                               ah_conv** out, char* err, int errlen) {
-  if (!out || !w || act < 0 || act > 2) {
+int ah_conv3x3_create_algo(int device, int C, int M, const uint16_t* w, const float* bias, int act, int algo,
+                           ah_conv** out, char* err, int errlen) {
+  if (algo == 0) return ah_conv3x3_create(device, C, M, w, bias, act, out, err, errlen);
+  if (!out || !w || act < 0 || act > 2 || (algo != 1 && algo != 2)) {
     CopyOut("invalid conv arguments", err, errlen);
     return 1;
   }
-  if (!ah::wino_supported(C, M)) {
-    CopyOut("Winograd conv supports C = 64, M = 64 (got C=" + std::to_string(C) + ", M=" + std::to_string(M) + ")",
+  const bool ok = algo == 1 ? ah::wino_supported(C, M) : ah::pair_supported(C, M);
+  if (!ok) {
+    CopyOut(std::string(algo == 1 ? "Winograd" : "two-SM") + " conv supports C = 64, M = 64 (got C=" +
+                std::to_string(C) + ", M=" + std::to_string(M) + ")",
             err, errlen);
     return 1;
   }
@@ -479,16 +485,18 @@ int ah_conv3x3_create_winograd(int device, int C, int M, const uint16_t* w, cons
   c->C = C;
   c->M = M;
   c->act = act;
-  c->wino = true;
+  c->wino = algo == 1;
+  c->pair = algo == 2;
   int sms = 0;
   if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) == cudaSuccess && sms > 0) c->num_sms = sms;
-  ce = ah::wino_upload(w, bias, C, M, &c->ww);
+  ce = c->wino ? ah::wino_upload(w, bias, C, M, &c->ww) : ah::pair_upload(w, bias, C, M, &c->pw);
   if (ce == cudaSuccess) ce = cudaMalloc(&c->status, sizeof(uint32_t));
   if (ce == cudaSuccess) ce = cudaMemset(c->status, 0, sizeof(uint32_t));
   if (ce != cudaSuccess) {
     CopyOut(std::string("conv weight upload failed: ") + cudaGetErrorString(ce), err, errlen);
     (void)cudaGetLastError();
     ah::wino_free(&c->ww);
+    ah::pair_free(&c->pw);
     if (c->status) cudaFree(c->status);
     return 1;
   }
@@ -505,7 +513,22 @@ int ah_conv3x3_run(ah_conv* c, const void* in, int H, int W, const void* add1, c
   cudaSetDevice(c->device);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   cudaError_t e;
-  if (c->wino) {
+  if (c->pair) {
+    if (c->plan_in != in || c->plan_out != out || c->plan_H != H || c->plan_W != W) {
+      std::string perr;
+      if (!ah::pair_plan(&c->pw, static_cast<const __half*>(in), H, W, static_cast<__half*>(out), c->num_sms,
+                         &c->pplan, &perr)) {
+        CopyOut(perr, err, errlen);
+        return 1;
+      }
+      c->plan_in = in;
+      c->plan_out = out;
+      c->plan_H = H;
+      c->plan_W = W;
+    }
+    e = ah::pair_launch(c->pplan, static_cast<const __half*>(add1), static_cast<const __half*>(add2), c->act,
+                        c->status, s);
+  } else if (c->wino) {
     if (c->plan_in != in || c->plan_out != out || c->plan_H != H || c->plan_W != W) {
       std::string perr;
       if (!ah::wino_plan(&c->ww, static_cast<const __half*>(in), H, W, static_cast<__half*>(out), c->num_sms,
@@ -551,7 +574,7 @@ int ah_conv3x3_run(ah_conv* c, const void* in, int H, int W, const void* add1, c
   return 0;
 }
 
-int ah_conv3x3_kind(ah_conv* c) { return c ? (c->wino ? 2 : (c->tc ? 0 : 1)) : -1; }
+int ah_conv3x3_kind(ah_conv* c) { return c ? (c->pair ? 3 : (c->wino ? 2 : (c->tc ? 0 : 1))) : -1; }
 
 int ah_conv3x3_status(ah_conv* c, uint32_t* status) {
   if (!c || !status) return 1;
@@ -568,6 +591,7 @@ void ah_conv3x3_destroy(ah_conv* c) {
   ah::conv_tc_free(&c->tcw);
   ah::simt_conv_free(&c->sw);
   ah::wino_free(&c->ww);
+  ah::pair_free(&c->pw);
   if (c->status) cudaFree(c->status);
   delete c;
 }

@@ -117,6 +117,31 @@ cudaError_t conv_tc_launch(const ConvTcPlan& plan, const __half* add1, const __h
 void conv_tc_set_test_hook(int wait_limit_ms, int stall_row);
 
 // ---------------------------------------------------------------------------
+// Two-SM (cta_group::2) vertical-window tensor-core convolution, 64 -> 64 channels, NHWC
+// fp16 output with the fused activation and up to two residual adds (conv_tc_pair.cu).
+// ---------------------------------------------------------------------------
+struct PairWeights {
+  void* wpack = nullptr;  // device: [2 CTA ranks][3 kx][320 rows][128 B] swizzled weight pieces
+  float* bias = nullptr;  // device: 64 fp32
+};
+struct PairPlan {
+  const PairWeights* w = nullptr;
+  int H = 0, W = 0;
+  __half* out = nullptr;
+  long long rows_total = 0;  // (256-pixel strips) x H
+  int grid_x = 0;            // 2 x clusters
+  CUtensorMap in_map, out_map32;
+};
+bool pair_supported(int C, int M);
+cudaError_t pair_upload(const uint16_t* w_oihw_f16, const float* bias_or_null, int C, int M, PairWeights* out);
+void pair_free(PairWeights* w);
+bool pair_plan(const PairWeights* w, const __half* in, int H, int W, __half* out, int num_sms, PairPlan* plan,
+               std::string* err);
+// out may be the last residual operand (in place: reduce-add stores, as conv_tc_launch).
+cudaError_t pair_launch(const PairPlan& plan, const __half* add1, const __half* add2, int act, uint32_t* status,
+                        cudaStream_t stream);
+
+// ---------------------------------------------------------------------------
 // Winograd F(2x2,3x3) tensor-core convolution, 64 -> 64 channels (conv_wino.cu): fp16
 // transformed operands (the reference's numerics), opt-in through the engine's conv
 // algorithm. NHWC fp16 output with the fused activation and up to two residual adds.

@@ -288,7 +288,8 @@ class Engine:
 
 class Conv3x3:
     """One fused 3x3 conv layer on device NHWC fp16 tensors (pointers as ints).
-    ``algo="winograd"`` selects the Winograd F(2x2,3x3) kernel (64 -> 64 channels)."""
+    ``algo``: "direct" (the default selection), "winograd" (Winograd F(2x2,3x3), 64 -> 64
+    channels) or "pair" (the direct conv on two SMs per MMA, 64 -> 64 channels)."""
 
     def __init__(self, weight_oihw: np.ndarray, bias: np.ndarray | None, act: int = 0, device: int = 0,
                  algo: str = "direct"):
@@ -298,16 +299,16 @@ class Conv3x3:
         b = None if bias is None else np.ascontiguousarray(bias.astype(np.float16).astype(np.float32))
         self._h = ctypes.c_void_p()
         err = _err()
-        create = self._lib.ah_conv3x3_create_winograd if algo == "winograd" else self._lib.ah_conv3x3_create
-        rc = create(device, c, m, w16.ctypes.data, None if b is None else b.ctypes.data, act, ctypes.byref(self._h),
-                    err, _ERR_LEN)
+        code = {"direct": 0, "winograd": 1, "pair": 2}[algo]
+        rc = self._lib.ah_conv3x3_create_algo(device, c, m, w16.ctypes.data, None if b is None else b.ctypes.data,
+                                              act, code, ctypes.byref(self._h), err, _ERR_LEN)
         if rc != 0:
             raise EngineHarnessError(_msg(err, "conv create failed"))
         self.C, self.M = c, m
 
     @property
     def kind(self) -> str:
-        return {0: "conv_tc", 1: "conv_simt", 2: "conv_wino"}[self._lib.ah_conv3x3_kind(self._h)]
+        return {0: "conv_tc", 1: "conv_simt", 2: "conv_wino", 3: "conv_pair"}[self._lib.ah_conv3x3_kind(self._h)]
 
     def run(self, in_ptr: int, h: int, w: int, out_ptr: int, add1: int = 0, add2: int = 0, stream: int = 0):
         err = _err()

@@ -48,8 +48,9 @@ def main(argv=None) -> int:
     ap.add_argument("--in-place", action="store_true",
                     help="write over the last residual operand (reduce-add stores); the "
                          "operand then accumulates across launches, which does not change the timing")
-    ap.add_argument("--algo", default="direct", choices=["direct", "winograd"],
-                    help="conv kernel: the direct implicit GEMM, or Winograd F(2x2,3x3) (64 -> 64 only)")
+    ap.add_argument("--algo", default="direct", choices=["direct", "winograd", "pair"],
+                    help="conv kernel: the direct implicit GEMM, Winograd F(2x2,3x3), or the direct conv on "
+                         "two SMs per MMA (the last two 64 -> 64 only)")
     ap.add_argument("--model", choices=["C4F32", "R8F64", "R16F96"],
                     help="time whole frames of this BASELINE chain (luma, 2x) at --H x --W through the "
                          "engine's CUDA graph instead of one layer (a small-frame case for profilers)")

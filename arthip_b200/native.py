@@ -57,7 +57,7 @@ SIGNATURES: dict[str, tuple] = {
     "ah_ep_compile_region": (_i32, [_vp, _i32, _i32, ctypes.POINTER(_vp), _cp, _i32]),
     "ah_ep_capability_destroy": (None, [_vp]),
     "ah_conv3x3_create": (_i32, [_i32, _i32, _i32, _vp, _vp, _i32, ctypes.POINTER(_vp), _cp, _i32]),
-    "ah_conv3x3_create_winograd": (_i32, [_i32, _i32, _i32, _vp, _vp, _i32, ctypes.POINTER(_vp), _cp, _i32]),
+    "ah_conv3x3_create_algo": (_i32, [_i32, _i32, _i32, _vp, _vp, _i32, _i32, ctypes.POINTER(_vp), _cp, _i32]),
     "ah_conv3x3_run": (_i32, [_vp, _vp, _i32, _i32, _vp, _vp, _vp, _vp, _cp, _i32]),
     "ah_conv3x3_kind": (_i32, [_vp]),
     "ah_conv3x3_status": (_i32, [_vp, _u32p]),

@@ -166,14 +166,17 @@ int ah_conv3x3_create(int device, int C, int M, const uint16_t* w_oihw_f16, cons
  * bit for bit. It must not overlap in_nhwc. */
 int ah_conv3x3_run(ah_conv* c, const void* in_nhwc, int H, int W, const void* add1, const void* add2,
                    void* out_nhwc, void* stream, char* err, int errlen);
-/* The same layer on the Winograd F(2x2,3x3) tcgen05 kernel (C = 64, M = 64 only; else
- * return 1): the reference's own algorithm and numerics (winograd_conv,
- * src/common/hip_kernels.h:143-396, weights U = G g G^T rounded to fp16,
- * src/vapoursynth/hip_engine.cc:972-1009). fp16 transformed operands make it less exact
- * than the direct kernel; run with ah_conv3x3_run. */
-int ah_conv3x3_create_winograd(int device, int C, int M, const uint16_t* w_oihw_f16, const float* bias, int act,
-                               ah_conv** out, char* err, int errlen);
-/* 0 = tcgen05 direct implicit GEMM, 1 = CUDA-core kernel, 2 = tcgen05 Winograd. */
+/* The same layer on a chosen kernel (C = 64, M = 64 for algo 1 and 2; else return 1):
+ * algo 0 = the default selection (as ah_conv3x3_create);
+ * algo 1 = Winograd F(2x2,3x3) on tcgen05 with the reference's numerics (winograd_conv,
+ *          src/common/hip_kernels.h:143-396; U = G g G^T rounded to fp16,
+ *          src/vapoursynth/hip_engine.cc:972-1009), less exact than the direct form;
+ * algo 2 = the direct vertical-window conv on two SMs per MMA (tcgen05 cta_group::2).
+ * Run with ah_conv3x3_run. */
+int ah_conv3x3_create_algo(int device, int C, int M, const uint16_t* w_oihw_f16, const float* bias, int act, int algo,
+                           ah_conv** out, char* err, int errlen);
+/* 0 = tcgen05 direct implicit GEMM, 1 = CUDA-core kernel, 2 = tcgen05 Winograd,
+ * 3 = tcgen05 direct on two SMs. */
 int ah_conv3x3_kind(ah_conv* c);
 /* Reads and clears the device error word the tensor-core kernel writes on a timed-out
  * pipeline wait (0 = none). Synchronises the device. */
