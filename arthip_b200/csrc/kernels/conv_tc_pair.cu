@@ -43,19 +43,23 @@ namespace ah {
 
 namespace {
 
-constexpr int kPThreads = 192;      // w0 producer, w1 TMEM + MMA issuer (even CTA), w2-5 epilogue
-constexpr int kPSlots = 4;          // input-row slots per CTA
+// Warps: 0 / 3 = TMA producers of pipe 0 / 1 (both CTAs); 1 / 2 = MMA issuers of pipe 0 / 1
+// (even CTA; warp 1 of both CTAs allocates TMEM); 4-7 / 8-11 = epilogues of pipe 0 / 1.
+// Two row pipelines per pair, as in the single-SM kernel: while one issuer waits on its
+// synchronisation chain, the other's MMAs keep the tensor cores busy.
+constexpr int kPThreads = 384;
+constexpr int kPSlots = 2;          // input-row slots per pipe and CTA
 constexpr int kPSlotBytes = 17408;  // 130 pixels x 128 B, 1024-aligned
 constexpr int kPPieceRows = 320;    // weight rows per kx (all pieces)
 constexpr int kPKxBytes = kPPieceRows * 128;
-constexpr int kPNacc = 8;           // accumulator chunks of 64 columns (all 512 TMEM columns)
+constexpr int kPNacc = 4;           // accumulator chunks of 64 columns per pipe (256 TMEM columns)
 constexpr int kPOffW = 0;
 constexpr int kPOffA = kPOffW + 3 * kPKxBytes;
-constexpr int kPOffOnes = kPOffA + kPSlots * kPSlotBytes;
+constexpr int kPOffOnes = kPOffA + 2 * kPSlots * kPSlotBytes;
 constexpr int kPOffBias = kPOffOnes + 4096;
 constexpr int kPOffStage = kPOffBias + 1024;
-constexpr int kPOffBars = kPOffStage + 4 * 2 * 2048;
-constexpr int kPSmem = kPOffBars + 512 + 1024;
+constexpr int kPOffBars = kPOffStage + 8 * 2 * 2048;
+constexpr int kPSmem = kPOffBars + 256 + 1024;
 
 // Row offset of the piece (a, n) inside a kx block.
 __host__ __device__ constexpr int piece_row(int a, int n) {
@@ -174,19 +178,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sW = smem + kPOffW;
-  uint8_t* sA = smem + kPOffA;
+  uint8_t* sA = smem + kPOffA;  // pipe p, slot s at sA + (p * kPSlots + s) * kPSlotBytes
   uint8_t* sOnes = smem + kPOffOnes;
   uint8_t* sBias = smem + kPOffBias;
   uint8_t* sStage = smem + kPOffStage;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kPOffBars);
-  uint64_t* full = bars;                     // [kPSlots], used in the even CTA
-  uint64_t* empty = full + kPSlots;          // [kPSlots], both CTAs
-  uint64_t* accf = empty + kPSlots;          // [kPNacc], both CTAs
-  uint64_t* acce = accf + kPNacc;            // [kPNacc], used in the even CTA (count 8)
-  uint64_t* wbar = acce + kPNacc;            // this CTA's weight half
+  uint64_t* full = bars;                     // [2][kPSlots], used in the even CTA
+  uint64_t* empty = full + 2 * kPSlots;      // [2][kPSlots], both CTAs
+  uint64_t* accf = empty + 2 * kPSlots;      // [2][kPNacc], both CTAs
+  uint64_t* acce = accf + 2 * kPNacc;        // [2][kPNacc], used in the even CTA (count 8)
+  uint64_t* wbar = acce + 2 * kPNacc;        // this CTA's weight half
   uint64_t* wpeer = wbar + 1;                // even CTA: the odd CTA's weights landed
-  uint64_t* donebar = wpeer + 1;             // even CTA: every MMA drained
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(donebar + 1);
+  uint64_t* donebar = wpeer + 1;             // [2] even CTA: every MMA of a pipe drained
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(donebar + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -196,21 +200,22 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
   ptx::griddep_launch_dependents();
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kPSlots; ++s) {
-      ptx::mbar_init(ptx::smem_u32(&full[s]), 1);
-      ptx::mbar_init(ptx::smem_u32(&empty[s]), 1);
+    for (int i = 0; i < 2 * kPSlots; ++i) {
+      ptx::mbar_init(ptx::smem_u32(&full[i]), 1);
+      ptx::mbar_init(ptx::smem_u32(&empty[i]), 1);
     }
-    for (int i = 0; i < kPNacc; ++i) {
+    for (int i = 0; i < 2 * kPNacc; ++i) {
       ptx::mbar_init(ptx::smem_u32(&accf[i]), 1);
-      ptx::mbar_init(ptx::smem_u32(&acce[i]), 8);  // 4 epilogue warps in each CTA
+      ptx::mbar_init(ptx::smem_u32(&acce[i]), 8);  // the pipe's 4 epilogue warps in each CTA
     }
     ptx::mbar_init(ptx::smem_u32(wbar), 1);
     ptx::mbar_init(ptx::smem_u32(wpeer), 1);
-    ptx::mbar_init(ptx::smem_u32(donebar), 1);
+    ptx::mbar_init(ptx::smem_u32(&donebar[0]), 1);
+    ptx::mbar_init(ptx::smem_u32(&donebar[1]), 1);
     *abort_flag = 0;
     ptx::fence_mbar_init();
   }
-  if (warp == 0 && lane == 0) ptx::prefetch_tensormap(&a.in_map);
+  if ((warp == 0 || warp == 3) && lane == 0) ptx::prefetch_tensormap(&a.in_map);
   if (warp == 1) {  // the pair's TMEM: the same warp of both CTAs, the same slot offset
     asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(ptx::smem_u32(tmem_slot)),
                  "r"(512)
@@ -238,38 +243,46 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
   ptx::tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
+  // The cluster's contiguous (256-pixel strip, row) range, split between the two pipes.
   const long long nclus = gridDim.x / 2;
   const long long cl = blockIdx.x / 2;
   const long long t0 = cl * a.rows_total / nclus;
   const long long t1 = (cl + 1) * a.rows_total / nclus;
+  const long long tm = (t0 + t1) / 2;
 
-  if (warp == 0) {
-    // ---------------- TMA producer (both CTAs) ----------------
+  if (warp == 0 || warp == 3) {
+    // ---------------- TMA producers (both CTAs) ----------------
+    const int pp = warp == 0 ? 0 : 1;
     if (lane == 0) {
-      ptx::mbar_arrive_expect_tx(ptx::smem_u32(wbar), 3 * kPKxBytes);
-      for (int kx = 0; kx < 3; ++kx)
-        ptx::bulk_load(ptx::smem_u32(sW + kx * kPKxBytes), a.wpack + (static_cast<size_t>(rank) * 3 + kx) * kPKxBytes,
-                       kPKxBytes, ptx::smem_u32(wbar));
       bool ok = true;
-      if (!lead) {  // tell the even issuer this half of the weights is in place
-        ok = ptx::mbar_wait(ptx::smem_u32(wbar), 0, abort_flag, a.wait_limit_ns);
-        if (ok) mbar_arrive_remote(map_to_rank(ptx::smem_u32(wpeer), 0));
+      if (pp == 0) {
+        ptx::mbar_arrive_expect_tx(ptx::smem_u32(wbar), 3 * kPKxBytes);
+        for (int kx = 0; kx < 3; ++kx)
+          ptx::bulk_load(ptx::smem_u32(sW + kx * kPKxBytes),
+                         a.wpack + (static_cast<size_t>(rank) * 3 + kx) * kPKxBytes, kPKxBytes, ptx::smem_u32(wbar));
+        if (!lead) {  // tell the even issuers this half of the weights is in place
+          ok = ptx::mbar_wait(ptx::smem_u32(wbar), 0, abort_flag, a.wait_limit_ns);
+          if (ok) mbar_arrive_remote(map_to_rank(ptx::smem_u32(wpeer), 0));
+        }
       }
       ptx::griddep_wait();  // the input rows come from the previous layer
-      const uint32_t full0 = map_to_rank(ptx::smem_u32(&full[0]), 0);
+      uint64_t* pfull = full + pp * kPSlots;
+      uint64_t* pempty = empty + pp * kPSlots;
+      uint8_t* pA = sA + static_cast<size_t>(pp) * kPSlots * kPSlotBytes;
+      const uint32_t full0 = map_to_rank(ptx::smem_u32(&pfull[0]), 0);
       uint32_t g = 0, slot = 0, phase = 0;
-      for (long long t = t0; t < t1 && ok;) {
+      for (long long t = pp == 0 ? t0 : tm, tend = pp == 0 ? tm : t1; t < tend && ok;) {
         const int strip = static_cast<int>(t / a.H), ya = static_cast<int>(t % a.H);
-        const int yb = static_cast<int>(std::min<long long>(a.H, ya + (t1 - t)));
+        const int yb = static_cast<int>(std::min<long long>(a.H, ya + (tend - t)));
         t = static_cast<long long>(strip) * a.H + yb;
         const int x0 = strip * 256 + 128 * static_cast<int>(rank) - 1;
         for (int r = ya - 1; r <= yb; ++r, ++g) {
-          if (!ptx::mbar_wait(ptx::smem_u32(&empty[slot]), phase ^ 1u, abort_flag, a.wait_limit_ns)) {
+          if (!ptx::mbar_wait(ptx::smem_u32(&pempty[slot]), phase ^ 1u, abort_flag, a.wait_limit_ns)) {
             ok = false;
             break;
           }
-          if (lead) ptx::mbar_arrive_expect_tx(ptx::smem_u32(&full[slot]), 2 * 130 * 128);
-          tma_load_3d_pair(ptx::smem_u32(sA + slot * kPSlotBytes), &a.in_map, full0 + slot * 8u, 0, x0, r);
+          if (lead) ptx::mbar_arrive_expect_tx(ptx::smem_u32(&pfull[slot]), 2 * 130 * 128);
+          tma_load_3d_pair(ptx::smem_u32(pA + slot * kPSlotBytes), &a.in_map, full0 + slot * 8u, 0, x0, r);
           if (++slot == kPSlots) {
             slot = 0;
             phase ^= 1u;
@@ -277,19 +290,25 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
         }
       }
       // No TMA write in flight at exit: the even CTA waits (bounded) on the last loads of
-      // both CTAs; the odd CTA's loads are covered by the cluster barrier after the even
-      // CTA's wait.
+      // both CTAs; the odd CTA's loads are covered by the cluster barrier after that wait.
       if (lead) {
         volatile int never_abort = 0;
         const uint32_t first = g > static_cast<uint32_t>(kPSlots) ? g - kPSlots : 0u;
         for (uint32_t j = first; j < g; ++j)
-          ptx::mbar_wait(ptx::smem_u32(&full[j % kPSlots]), (j / kPSlots) & 1u, &never_abort, a.wait_limit_ns);
+          ptx::mbar_wait(ptx::smem_u32(&pfull[j % kPSlots]), (j / kPSlots) & 1u, &never_abort, a.wait_limit_ns);
       }
     }
-  } else if (warp == 1) {
-    // ---------------- MMA issuer (even CTA) ----------------
+  } else if (warp == 1 || warp == 2) {
+    // ---------------- MMA issuers (even CTA) ----------------
+    const int pp = warp - 1;
     if (lane == 0 && lead) {
-      const uint32_t sA_u = ptx::smem_u32(sA), sW_u = ptx::smem_u32(sW);
+      uint64_t* pfull = full + pp * kPSlots;
+      uint64_t* pempty = empty + pp * kPSlots;
+      uint64_t* paccf = accf + pp * kPNacc;
+      uint64_t* pacce = acce + pp * kPNacc;
+      const uint32_t tbase = tmem_base + pp * 256;
+      const uint32_t sA_u = ptx::smem_u32(sA + static_cast<size_t>(pp) * kPSlots * kPSlotBytes);
+      const uint32_t sW_u = ptx::smem_u32(sW);
       const uint32_t ones_lo = ptx::desc_lo(ptx::smem_u32(sOnes)), bias_lo = ptx::desc_lo(ptx::smem_u32(sBias));
       const uint32_t hi32 = ptx::desc_hi(256, 6), hi128 = ptx::desc_hi(1024, 2);
       const uint32_t alo0 = ptx::desc_lo(sA_u);
@@ -299,44 +318,52 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
       bool ok = ptx::mbar_wait(ptx::smem_u32(wbar), 0, abort_flag, a.wait_limit_ns);
       if (ok) ok = ptx::mbar_wait(ptx::smem_u32(wpeer), 0, abort_flag, a.wait_limit_ns);
       uint32_t obase = 0, slot = 0, phase = 0;
-      for (long long t = t0; t < t1 && ok;) {
+      for (long long t = pp == 0 ? t0 : tm, tend = pp == 0 ? tm : t1; t < tend && ok;) {
         const int strip = static_cast<int>(t / a.H), ya = static_cast<int>(t % a.H);
-        const int yb = static_cast<int>(std::min<long long>(a.H, ya + (t1 - t)));
+        const int yb = static_cast<int>(std::min<long long>(a.H, ya + (tend - t)));
         t = static_cast<long long>(strip) * a.H + yb;
-        (void)strip;
         const int n = yb - ya;
         for (int j = 0; j <= n + 1 && ok; ++j) {
-          ok = ptx::mbar_wait(ptx::smem_u32(&full[slot]), phase, abort_flag, a.wait_limit_ns);
+          ok = ptx::mbar_wait(ptx::smem_u32(&pfull[slot]), phase, abort_flag, a.wait_limit_ns);
           const int ky_lo = max(0, j - (n - 1)), ky_hi = min(2, j);
           if (ok && ky_lo == 0) {  // output row j starts here: bias-initialise its chunk
             const uint32_t o = obase + j, c = (NCH - (o & (NCH - 1))) & (NCH - 1);
-            ok = ptx::mbar_wait(ptx::smem_u32(&acce[c]), ((o >> 3) & 1u) ^ 1u, abort_flag, a.wait_limit_ns);
+            ok = ptx::mbar_wait(ptx::smem_u32(&pacce[c]), ((o >> 2) & 1u) ^ 1u, abort_flag, a.wait_limit_ns);
             ptx::tc_fence_after();
-            if (ok) mma_pair(tmem_base + c * 64, ones_lo, hi32, bias_lo, hi32, id_bias, 0);
+            if (ok) mma_pair(tbase + c * 64, ones_lo, hi32, bias_lo, hi32, id_bias, 0);
           }
           if (!ok) break;
           const uint32_t ohi = obase + j - ky_lo;
           const uint32_t chi = (NCH - (ohi & (NCH - 1))) & (NCH - 1);
           const uint32_t span = ky_hi - ky_lo + 1;
           const uint32_t n1 = min(span, NCH - chi), n2 = span - n1;
-          const uint32_t d1 = tmem_base + chi * 64, d2 = tmem_base;
+          const uint32_t d1 = tbase + chi * 64, d2 = tbase;
           const uint32_t i1 = ptx::idesc_f16_f32(256, n1 * 64), i2 = ptx::idesc_f16_f32(256, (n2 ? n2 : 1) * 64);
           const uint32_t p1 = static_cast<uint32_t>(piece_row(ky_lo, n1)) * 8u;  // rows x 128 B in 16-B units
           const uint32_t p2 = n2 ? static_cast<uint32_t>(piece_row(ky_lo + n1, n2)) * 8u : 0u;
           const uint32_t sl = alo0 + slot * (kPSlotBytes >> 4);
+          if (n2 == 0) {  // one branch per row, none per MMA
 #pragma unroll
-          for (int kx = 0; kx < 3; ++kx)
+            for (int kx = 0; kx < 3; ++kx)
 #pragma unroll
-            for (int kb = 0; kb < 4; ++kb) {
-              const uint32_t alo = sl + ((kx * 128 + kb * 32) >> 4);
-              const uint32_t wb = wlo0 + ((kx * kPKxBytes + kb * 32) >> 4);
-              mma_pair(d1, alo, hi128, wb + p1, hi128, i1, 1);
-              if (n2) mma_pair(d2, alo, hi128, wb + p2, hi128, i2, 1);
-            }
-          commit_pair_both(ptx::smem_u32(&empty[slot]));
+              for (int kb = 0; kb < 4; ++kb)
+                mma_pair(d1, sl + ((kx * 128 + kb * 32) >> 4), hi128, wlo0 + ((kx * kPKxBytes + kb * 32) >> 4) + p1,
+                         hi128, i1, 1);
+          } else {
+#pragma unroll
+            for (int kx = 0; kx < 3; ++kx)
+#pragma unroll
+              for (int kb = 0; kb < 4; ++kb) {
+                const uint32_t alo = sl + ((kx * 128 + kb * 32) >> 4);
+                const uint32_t wb = wlo0 + ((kx * kPKxBytes + kb * 32) >> 4);
+                mma_pair(d1, alo, hi128, wb + p1, hi128, i1, 1);
+                mma_pair(d2, alo, hi128, wb + p2, hi128, i2, 1);
+              }
+          }
+          commit_pair_both(ptx::smem_u32(&pempty[slot]));
           if (ky_hi == 2) {  // output row j-2 received its last kernel row
             const uint32_t o = obase + j - 2, c = (NCH - (o & (NCH - 1))) & (NCH - 1);
-            commit_pair_both(ptx::smem_u32(&accf[c]));
+            commit_pair_both(ptx::smem_u32(&paccf[c]));
           }
           if (++slot == kPSlots) {
             slot = 0;
@@ -345,24 +372,27 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
         }
         obase += n;
       }
-      commit_pair_local(ptx::smem_u32(donebar));
+      commit_pair_local(ptx::smem_u32(&donebar[pp]));
       volatile int never_abort = 0;
-      ptx::mbar_wait(ptx::smem_u32(donebar), 0, &never_abort, a.wait_limit_ns);
+      ptx::mbar_wait(ptx::smem_u32(&donebar[pp]), 0, &never_abort, a.wait_limit_ns);
     }
     __syncwarp();
   } else {
-    // ---------------- epilogue (warps 2-5, both CTAs) ----------------
+    // ---------------- epilogues (warps 4-7: pipe 0, 8-11: pipe 1; both CTAs) ----------------
     ptx::griddep_wait();  // residual operands and the output buffer belong to earlier layers
-    const int q = warp & 3;       // TMEM lane quarter this warp may access
-    const int e = warp - 2;
+    const int e = warp - 4;
+    const int pp = e >> 2;
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
     uint8_t* stage = sStage + e * 2 * 2048;
-    const uint32_t acce0 = map_to_rank(ptx::smem_u32(&acce[0]), 0);
+    const uint32_t tbase = tmem_base + pp * 256;
+    uint64_t* paccf = accf + pp * kPNacc;
+    const uint32_t acce0 = map_to_rank(ptx::smem_u32(&acce[pp * kPNacc]), 0);
     uint32_t acc_cnt = 0;
     bool ok = true;
     bool stores_pending = false;
-    for (long long t = t0; t < t1 && ok;) {
+    for (long long t = pp == 0 ? t0 : tm, tend = pp == 0 ? tm : t1; t < tend && ok;) {
       const int strip = static_cast<int>(t / a.H), ya = static_cast<int>(t % a.H);
-      const int yb = static_cast<int>(std::min<long long>(a.H, ya + (t1 - t)));
+      const int yb = static_cast<int>(std::min<long long>(a.H, ya + (tend - t)));
       t = static_cast<long long>(strip) * a.H + yb;
       const int xw = strip * 256 + 128 * static_cast<int>(rank) + q * 32;
       const int x = xw + lane;
@@ -391,7 +421,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
         }
         int w_ok = 0;
         if (lane == 0)
-          w_ok = ptx::mbar_wait(ptx::smem_u32(&accf[acc]), (acc_cnt >> 3) & 1u, abort_flag, a.wait_limit_ns) ? 1 : 0;
+          w_ok = ptx::mbar_wait(ptx::smem_u32(&paccf[acc]), (acc_cnt >> 2) & 1u, abort_flag, a.wait_limit_ns) ? 1 : 0;
         w_ok = __shfl_sync(0xffffffffu, w_ok, 0);
         if (!w_ok) {
           ok = false;
@@ -405,7 +435,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
         uint32_t rrs[2][32];
 #pragma unroll
         for (int g = 0; g < 2; ++g)
-          ptx::tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * 64 + g * 32, rrs[g]);
+          ptx::tmem_ld_32x32b_x32(tbase + (static_cast<uint32_t>(q * 32) << 16) + acc * 64 + g * 32, rrs[g]);
         ptx::tmem_wait_ld();
         ptx::tc_fence_before();
         __syncwarp();
