@@ -31,6 +31,7 @@ cpu_baseline / --impl reference: the reference's CPU path (ONNX Runtime CPU is n
 from __future__ import annotations
 
 import argparse
+import contextlib
 import json
 import os
 import statistics
@@ -96,19 +97,29 @@ def load_peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clock/throttle sampling during the timed region."""
+    """nvidia-smi clock/throttle sampling during the timed region.
+
+    nvidia-smi takes up to a second to print its first sample (longer when every rank
+    starts one at once), which is longer than a short timed region. So the sampler is
+    started before the warm-up, ``wait_first()`` blocks (bounded) until it has printed a
+    row, and ``window()`` marks the timed region: ``summary()`` keeps the rows read inside
+    it, or, when the region was shorter than one interval, the first row read after it."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    INTERVAL_MS = 100
 
     def __init__(self, gpu_id: str | None):
-        self.rows = []
+        self.rows = []  # (monotonic time read, fields)
         self.proc = None
         self.gpu_id = gpu_id
+        self.t0 = self.t1 = None
+        self._first = threading.Event()
 
-    def __enter__(self):
-        cmd = ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200"]
+    def start(self):
+        cmd = ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+               "-lms", str(self.INTERVAL_MS)]
         if self.gpu_id:
             cmd += ["-i", self.gpu_id]
         try:
@@ -119,22 +130,57 @@ class ClockSampler:
             self.proc = None
         return self
 
+    def wait_first(self, timeout_s: float = 10.0):
+        if self.proc:
+            self._first.wait(timeout_s)
+
+    def __enter__(self):
+        return self.start()
+
     def _read(self):
         for line in self.proc.stdout:
             parts = [p.strip() for p in line.split(",")]
             if len(parts) >= 9:
-                self.rows.append(parts)
+                self.rows.append((time.monotonic(), parts))
+                self._first.set()
 
-    def __exit__(self, *a):
+    @contextlib.contextmanager
+    def window(self):
+        self.t0 = time.monotonic()
+        try:
+            yield self
+        finally:
+            self.t1 = time.monotonic()
+            # one more interval, so that a region shorter than the interval still gets the
+            # sample taken while it ran
+            deadline = self.t1 + 3 * self.INTERVAL_MS / 1000.0
+            while self.proc and time.monotonic() < deadline and not any(t > self.t1 for t, _ in self.rows):
+                time.sleep(0.01)
+
+    def stop(self):
         if self.proc:
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
             except Exception:
                 self.proc.kill()
+            self.proc = None
+
+    def __exit__(self, *a):
+        self.stop()
+
+    def _selected(self):
+        if self.t0 is None:
+            return [r for _, r in self.rows]
+        inside = [r for t, r in self.rows if self.t0 <= t <= self.t1]
+        if inside:
+            return inside
+        after = [r for t, r in self.rows if t > self.t1]
+        return after[:1]
 
     def summary(self):
-        if not self.rows:
+        rows = self._selected()
+        if not rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
 
         def num(x):
@@ -142,13 +188,22 @@ class ClockSampler:
                 return float(x)
             except ValueError:
                 return None
-        sm = [num(r[1]) for r in self.rows if num(r[1]) is not None]
-        mx = [num(r[2]) for r in self.rows if num(r[2]) is not None]
+        sm = [num(r[1]) for r in rows if num(r[1]) is not None]
+        mx = [num(r[2]) for r in rows if num(r[2]) is not None]
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in self.rows for i in range(4) if r[5 + i].lower().startswith("active")})
-        pw = [num(r[3]) for r in self.rows if num(r[3]) is not None]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower().startswith("active")})
+        pw = [num(r[3]) for r in rows if num(r[3]) is not None]
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": reasons, "samples": len(self.rows), "power_w_max": max(pw) if pw else None}
+                "reasons": reasons, "samples": len(rows), "power_w_max": max(pw) if pw else None}
+
+
+def _gpu_uuid(dev) -> str | None:
+    """The device's UUID in nvidia-smi's form, so that each rank samples its own GPU."""
+    import torch
+    try:
+        return "GPU-" + str(torch.cuda.get_device_properties(dev).uuid)
+    except Exception:
+        return None
 
 
 def dist_setup(backend: str = "nccl"):
@@ -339,19 +394,29 @@ def run_frame_split(args):
 
             def one():
                 eng.enqueue()
-        for _ in range(args.warmup):
-            one()
-        eng.synchronize()
-        torch.cuda.synchronize()
-        dist_barrier(world)
-        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        ev0.record(estream)
-        for _ in range(steps):
-            one()
-        ev1.record(estream)
-        eng.synchronize()
-        torch.cuda.synchronize()
-        ms = dist_max(ev0.elapsed_time(ev1) / steps, world)
+        clk = ClockSampler(_gpu_uuid(dev)).start()
+        try:
+            for _ in range(args.warmup):
+                one()
+            eng.synchronize()
+            torch.cuda.synchronize()
+            clk.wait_first()
+            dist_barrier(world)
+            ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            with clk.window():
+                ev0.record(estream)
+                for _ in range(steps):
+                    one()
+                ev1.record(estream)
+                eng.synchronize()
+                torch.cuda.synchronize()
+        finally:
+            clk.stop()
+        my_ms = ev0.elapsed_time(ev1) / steps
+        ms = dist_max(my_ms, world)
+        clocks = clk.summary()
+        per_rank = dist_gather({"rank": rank, "ms": my_ms, "strip_rows": strip_rows, "sm_mhz": clocks["sm_mhz"],
+                                "reasons": clocks["reasons"], "power_w_max": clocks.get("power_w_max")}, world)
         dist_barrier(world)
     if rank == 0:
         split = (f"{world} row strips, {halo}-row recompute halo each side, no exchange" if args.halo == "recompute"
@@ -362,7 +427,10 @@ def run_frame_split(args):
             "n_gpus": world, "steps": steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": False,
             "scaling": "strong", "vs_baseline": None, "dtype": "fp16", "data": "synthetic",
             "config": {"workload": "C4 (second part): one 7680x4320 luma frame, R8F64", "split": split,
-                       "halo_mode": args.halo, "strip_rows_rank0": strip_rows}})
+                       "halo_mode": args.halo, "strip_rows_rank0": strip_rows},
+            "clocks": {"sm_mhz": clocks["sm_mhz"], "sm_max_mhz": clocks["sm_max_mhz"], "reasons": clocks["reasons"],
+                       "samples": clocks["samples"]},
+            "per_rank": per_rank})
     if world > 1:
         import torch.distributed as dist
         dist.destroy_process_group()
@@ -435,28 +503,29 @@ def main():
                 dst.copy_(ring[i % 8], non_blocking=True)
             eng.enqueue()
 
-        for i in range(args.warmup):
-            step(i)
-        eng.synchronize()
-
-        gpu_uuid = None
+        # the clock sampler starts before the warm-up so that its first sample is out by
+        # the time the timed region begins
+        clk = ClockSampler(_gpu_uuid(dev)).start()
         try:
-            gpu_uuid = "GPU-" + str(torch.cuda.get_device_properties(dev).uuid)
-        except Exception:
-            pass
-
-        # -------- timed region: K frames through the captured CUDA graph --------
-        dist_barrier(world)
-        torch.cuda.synchronize()
-        ev0 = torch.cuda.Event(enable_timing=True)
-        ev1 = torch.cuda.Event(enable_timing=True)
-        with ClockSampler(gpu_uuid) as clk:
-            ev0.record(estream)
-            for i in range(args.steps):
+            for i in range(args.warmup):
                 step(i)
-            ev1.record(estream)
             eng.synchronize()
+            clk.wait_first()
+
+            # -------- timed region: K frames through the captured CUDA graph --------
+            dist_barrier(world)
             torch.cuda.synchronize()
+            ev0 = torch.cuda.Event(enable_timing=True)
+            ev1 = torch.cuda.Event(enable_timing=True)
+            with clk.window():
+                ev0.record(estream)
+                for i in range(args.steps):
+                    step(i)
+                ev1.record(estream)
+                eng.synchronize()
+                torch.cuda.synchronize()
+        finally:
+            clk.stop()
         dist_barrier(world)
         span_max = dist_max(ev0.elapsed_time(ev1), world)
         frames = args.steps

@@ -67,3 +67,69 @@ def test_reference_arm_line_on_rank0():
     assert line["impl"] == "reference" and line["unit"] == "frames/s" and line["value"] > 0
     assert line["cpu_baseline"]["kind"] == "port" and line["cpu_baseline"]["cores"] >= 1
     assert line["e2e"]["h2d_bytes_per_step"] == 0 and line["e2e"]["d2h_bytes_per_step"] == 0
+
+
+def _fake_smi(tmp_path: Path, monkeypatch):
+    """An `nvidia-smi` on PATH that prints one CSV row every 20 ms with a rising SM clock
+    and sw_power_cap active, as `--query-gpu ... -lms` does."""
+    smi = tmp_path / "nvidia-smi"
+    smi.write_text(
+        f"#!{sys.executable}\n"
+        "import sys, time\n"
+        "i = 0\n"
+        "while True:\n"
+        "    print(f'0, {1000 + i}, 1965, 700.5, 0x4, Not Active, Not Active, Not Active, Active', flush=True)\n"
+        "    i += 1\n"
+        "    time.sleep(0.02)\n")
+    smi.chmod(0o755)
+    monkeypatch.setenv("PATH", f"{tmp_path}{os.pathsep}{os.environ.get('PATH', '')}")
+
+
+def test_clock_sampler_keeps_only_the_timed_window(tmp_path, monkeypatch):
+    import time
+    sys.path.insert(0, str(ROOT))
+    import bench
+    _fake_smi(tmp_path, monkeypatch)
+    clk = bench.ClockSampler(None).start()
+    try:
+        clk.wait_first(10.0)
+        assert clk.rows, "the sampler saw no row before the window"
+        time.sleep(0.2)
+        with clk.window():
+            time.sleep(0.3)
+        time.sleep(0.2)
+    finally:
+        clk.stop()
+    s = clk.summary()
+    inside = [float(r[1]) for t, r in clk.rows if clk.t0 <= t <= clk.t1]
+    assert s["samples"] == len(inside) >= 3
+    assert len(clk.rows) > s["samples"]  # rows before and after the window are dropped
+    assert min(inside) <= s["sm_mhz"] <= max(inside)
+    assert s["sm_max_mhz"] == 1965.0 and s["reasons"] == ["sw_power_cap"] and s["power_w_max"] == 700.5
+
+
+def test_clock_sampler_short_window_takes_the_next_row(tmp_path, monkeypatch):
+    sys.path.insert(0, str(ROOT))
+    import bench
+    _fake_smi(tmp_path, monkeypatch)
+    clk = bench.ClockSampler(None).start()
+    try:
+        clk.wait_first(10.0)
+        with clk.window():
+            pass
+    finally:
+        clk.stop()
+    s = clk.summary()
+    assert s["samples"] >= 1 and s["sm_mhz"] is not None and s["reasons"] == ["sw_power_cap"]
+
+
+def test_clock_sampler_without_nvidia_smi_reports_unsampled(tmp_path, monkeypatch):
+    sys.path.insert(0, str(ROOT))
+    import bench
+    monkeypatch.setenv("PATH", str(tmp_path))
+    clk = bench.ClockSampler(None).start()
+    clk.wait_first(0.5)
+    with clk.window():
+        pass
+    clk.stop()
+    assert clk.summary() == {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
