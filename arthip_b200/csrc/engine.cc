@@ -999,6 +999,7 @@ bool Engine::EnsureBuilt(const std::vector<int64_t>& s4, std::string& error) {
           to.clip = d.sout.clip;
           to.clip_lo = d.sout.clip_lo;
           to.clip_hi = d.sout.clip_hi;
+          to.adds = (d.add_buf[0] >= 0 ? 1 : 0) + (d.add_buf[1] >= 0 ? 1 : 0);
           std::string perr;
           if (!conv_tc_plan(&cw.tcw, static_cast<const __half*>(bufs_[d.in_buf]), d.H, d.W, to, num_sms_, &d.tc,
                             &perr)) {

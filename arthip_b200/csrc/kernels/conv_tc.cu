@@ -155,6 +155,13 @@ size_t conv_tc_pack_layout(int C, int M, ConvTcWeights* L) {
       L->gofs[b * L->nchunks + k] = off;
       off += static_cast<long long>(rows) * L->chunk[k].rowbytes;
     }
+  // Four-channel convs (the 2x DepthToSpace tails of luma models) also get the kx-in-N
+  // blocks: 3 x 16 rows per chunk.
+  L->kxn = (L->vert && M == 4 && Mp == 16 && L->vmt == 16) ? 1 : 0;
+  for (int k = 0; k < L->nchunks; ++k) {
+    L->kxn_gofs[k] = L->kxn ? off : 0;
+    if (L->kxn) off += 3LL * 16 * L->chunk[k].rowbytes;
+  }
   L->wpack_bytes = static_cast<size_t>(off);
   return L->wpack_bytes;
 }
@@ -184,6 +191,22 @@ void conv_tc_pack_into(const uint16_t* w_oihw, const ConvTcWeights& L, uint8_t* 
         }
       }
     }
+  }
+  if (!L.kxn) return;
+  // kx-in-N blocks: row ky * 16 + kx * 4 + m holds w[m][.][ky][kx] (rows 12..15 of each
+  // kernel row stay zero).
+  for (int k = 0; k < L.nchunks; ++k) {
+    const ConvTcChunk& ch = L.chunk[k];
+    uint8_t* blk = img + L.kxn_gofs[k];
+    for (int ky = 0; ky < 3; ++ky)
+      for (int kx = 0; kx < 3; ++kx)
+        for (int m = 0; m < M; ++m) {
+          const int r = ky * 16 + kx * 4 + m;
+          for (int kk = 0; kk < ch.cw; ++kk) {
+            const uint16_t v = w_oihw[(static_cast<size_t>(m) * C + ch.c0 + kk) * 9 + ky * 3 + kx];
+            std::memcpy(blk + swz_granule(r, (kk * 2) / 16, ch.rowbytes) + (kk * 2) % 16, &v, 2);
+          }
+        }
   }
 }
 
@@ -233,6 +256,7 @@ bool conv_tc_plan(const ConvTcWeights* w, const __half* in, int H, int W, const 
   P->H = H;
   P->W = W;
   P->out = out;
+  P->kxn = 0;
   const int slot_bytes = slot_bytes_of(w);
   P->slot_bytes = slot_bytes;
   const bool vert = w->vert != 0;
@@ -249,6 +273,27 @@ bool conv_tc_plan(const ConvTcWeights* w, const __half* in, int H, int W, const 
     if (dual) {
       chosen = w->vmt;
       slots = 2;
+      // The kx-in-N form of the tail, for a launch without residual operands
+      // (ARTHIP_TAIL_KXN=0 keeps the three-kx form; read when the plan is built, never at
+      // launch). Its slots are 128 rows, its weights one block per chunk: as many slots
+      // as fit in half of the SM's shared memory.
+      const char* v = std::getenv("ARTHIP_TAIL_KXN");
+      if (w->kxn && out.adds == 0 && !(v && *v == '0')) {
+        int kslot = 0, kw = 0;
+        for (int k = 0; k < w->nchunks; ++k) {
+          kslot += kTcTilePx * w->chunk[k].rowbytes;
+          kw += round_up(3 * w->vmt * w->chunk[k].rowbytes, 1024);
+        }
+        int ks = 0;
+        for (int s2 = kMaxSlots; s2 >= 2 && !ks; --s2)
+          if (kw + 2 * s2 * kslot + 4096 + round_up(w->vmt * 32, 1024) + kTailBytes + 1024 <= kSmemPerSm / 2 - 1024)
+            ks = s2;
+        if (ks) {
+          P->kxn = 1;
+          slots = ks;
+          P->slot_bytes = kslot;
+        }
+      }
     }
     for (int s = kMaxSlots; s >= min_slots && !chosen; --s)
       if (smem_need(w, w->vmt, true, out.mode, s) <= kSmemLimit) {
@@ -284,13 +329,13 @@ bool conv_tc_plan(const ConvTcWeights* w, const __half* in, int H, int W, const 
   P->n_msplit = w->Mpad / chosen;
   P->nslots = slots;
   int off = 0;
-  for (int b = 0; b < (vert ? 3 : 9); ++b)
+  for (int b = 0; b < (P->kxn ? 1 : (vert ? 3 : 9)); ++b)
     for (int k = 0; k < w->nchunks; ++k) {
       P->wofs[b * w->nchunks + k] = off;
       off += round_up((vert ? 3 : 1) * chosen * w->chunk[k].rowbytes, 1024);
     }
   P->w_smem_bytes = off;
-  off += (vert ? 2 : 1) * slots * slot_bytes;
+  off += (vert ? 2 : 1) * slots * P->slot_bytes;
   P->ones_off = off;
   off += 4096;
   P->biasb_off = off;
@@ -321,8 +366,9 @@ bool conv_tc_plan(const ConvTcWeights* w, const __half* in, int H, int W, const 
   if (gx > rows_total) gx = rows_total;
   P->grid_x = static_cast<int>(gx);
 
+  // (the kx-in-N tail loads 32-pixel sub-tiles)
   for (int k = 0; k < w->nchunks; ++k)
-    if (!encode(enc, &P->maps[k], in, w->C, W, H, w->chunk[k].cw, kTcBoxPx, err)) return false;
+    if (!encode(enc, &P->maps[k], in, w->C, W, H, w->chunk[k].cw, P->kxn ? kKxnSub : kTcBoxPx, err)) return false;
   if (out.mode == 0) {
     if (chosen >= 32 && !encode(enc, &P->out_map32, out.ptr, w->M, W, H, 32, 32, err)) return false;
     if (chosen % 32 == 16 && !encode(enc, &P->out_map16, out.ptr, w->M, W, H, 16, 32, err)) return false;
@@ -397,7 +443,7 @@ cudaError_t conv_tc_launch(const ConvTcPlan& P, const __half* add1, const __half
   for (int k = 0; k < w->nchunks; ++k) {
     a.c0[k] = w->chunk[k].c0;
     a.slot_off[k] = w->chunk[k].slot_off;
-    tx += w->chunk[k].rowbytes * kTcBoxPx;
+    tx += w->chunk[k].rowbytes * (P.kxn ? kTcTilePx : kTcBoxPx);  // kx-in-N: 4 x 32-pixel sub-tiles
   }
   a.slot_bytes = P.slot_bytes;
   a.slot_tx = tx;
@@ -407,6 +453,7 @@ cudaError_t conv_tc_launch(const ConvTcPlan& P, const __half* add1, const __half
   a.biasb_off = P.biasb_off;
   a.stage_off = P.stage_off;
   a.stage_per_warp = P.stage_per_warp;
+  // (the strips of the kx-in-N tail advance by kKxnStride pixels; set with its variant below)
   a.rows_total = static_cast<long long>((P.W + kTcTilePx - 1) / kTcTilePx) * P.H;
   a.act = act;
   a.nacc = P.nacc;
@@ -431,7 +478,16 @@ cudaError_t conv_tc_launch(const ConvTcPlan& P, const __half* add1, const __half
   } else if (P.out.dts_b == 2 && (P.out.nchw || w->M == 4) && !a.add1 && P.n_msplit == 1 && w->M % 4 == 0 &&
              w->M <= 16 && w->M <= P.MT) {
     variant = 3;
+    if (P.kxn) {
+      // kx-in-N tail: one weight block per chunk, strips of kKxnStride pixels
+      variant = 6;
+      for (int k = 0; k < w->nchunks; ++k) a.gofs[k] = w->kxn_gofs[k];
+      a.rows_total = static_cast<long long>((P.W + kKxnStride - 1) / kKxnStride) * P.H;
+    }
   }
+  // A kx-in-N plan (tensor maps, slot layout) serves only that variant: it is built for
+  // launches without residual operands.
+  if (P.kxn && variant != 6) return cudaErrorInvalidValue;
   // Programmatic dependent launch: this kernel's set-up (barriers, TMEM, weights) overlaps
   // the previous kernel's last CTAs; it waits in hardware (griddepcontrol.wait) before it
   // reads the previous layers' activations or writes its output. ARTHIP_NO_PDL=1 turns it off.

@@ -60,7 +60,7 @@ constexpr int kSmemLimit = 232448;  // 227 KB opt-in dynamic shared memory per b
 constexpr int kStageTile = 2048;    // one 32-pixel x 32-channel fp16 staging tile
 constexpr int kTailBytes = 1024;    // barriers and flags
 constexpr int kSmemPerSm = 233472;  // shared memory of one SM (two CTAs share it)
-constexpr int kVariants = 6;        // EPI 0 x ACT {none, relu, silu}; EPI 1; EPI 2; SiLU wide
+constexpr int kVariants = 7;        // EPI 0 x ACT {none, relu, silu}; EPI 1; EPI 2; SiLU wide; EPI 3
 
 struct ConvTcArgs {
   CUtensorMap maps[kTcMaxChunks];
@@ -107,7 +107,8 @@ typedef void (*KernelFn)(ConvTcArgs);
 // The instantiation for an input channel count (C % 16 == 0, 16 <= C <= 128), a
 // formulation (vertical window, or standard) and an output variant (0-2: NHWC with act
 // none/relu/silu, 3: 2x DepthToSpace tail, 4: general per-element output; vertical window
-// only: 5 = 2 with eight epilogue warps per pipe, 640 threads).
+// only: 5 = 2 with eight epilogue warps per pipe, 640 threads; 6 = the kx-in-N 2x
+// DepthToSpace tail of four conv channels).
 KernelFn kernel_for(int C, bool vert, int variant);
 
 struct Segment {
@@ -232,13 +233,17 @@ struct ChunkCfg {
   __host__ __device__ static constexpr uint32_t layout(int k) { return rb(k) == 128 ? 2u : (rb(k) == 64 ? 4u : 6u); }
   __host__ __device__ static constexpr int area(int k) { return (136 * rb(k) + 1023) / 1024 * 1024; }
   __host__ __device__ static constexpr int off(int k) { return k == 0 ? 0 : off(k - 1) + area(k - 1); }
+  // Slot layout of the kx-in-N tail: four 32-pixel sub-tiles (128 rows) per chunk.
+  __host__ __device__ static constexpr int off128(int k) { return k == 0 ? 0 : off128(k - 1) + 128 * rb(k - 1); }
   __host__ __device__ static constexpr uint32_t hi(int k) { return ptx::desc_hi(8u * rb(k), layout(k)); }
 };
 
 // The MMAs of one input row in the vertical-window formulation: for every (chunk, kx,
 // k-block) one MMA of N = n1 * M into the window's first TMEM run and, where the window
 // wraps around the accumulator ring (SPLIT), a second one into the run at column 0.
-template <class Cfg, bool SPLIT>
+// NKX = 1 is the kx-in-N tail: one weight block per chunk holds all three kx, and the A
+// operand is the slot's 128 rows (four 32-pixel sub-tiles).
+template <class Cfg, bool SPLIT, int NKX = 3>
 __device__ __forceinline__ void vert_row_mmas(uint32_t sl, const uint32_t (&bv)[3][Cfg::N], uint32_t M,
                                               uint32_t ky_lo, uint32_t n1, uint32_t d1, uint32_t d2, uint32_t i1,
                                               uint32_t i2) {
@@ -247,10 +252,10 @@ __device__ __forceinline__ void vert_row_mmas(uint32_t sl, const uint32_t (&bv)[
     const uint32_t mrows16 = (M * Cfg::rb(k)) >> 4;  // M weight rows, in 16-byte units
     const uint32_t b1 = ky_lo * mrows16, b2 = (ky_lo + n1) * mrows16;
 #pragma unroll
-    for (int kx = 0; kx < 3; ++kx)
+    for (int kx = 0; kx < NKX; ++kx)
 #pragma unroll
       for (int kb = 0; kb < Cfg::kblocks(k); ++kb) {
-        const uint32_t alo = sl + ((Cfg::off(k) + kx * Cfg::rb(k) + kb * 32) >> 4);
+        const uint32_t alo = sl + (((NKX == 1 ? Cfg::off128(k) : Cfg::off(k)) + kx * Cfg::rb(k) + kb * 32) >> 4);
         const uint32_t blo = bv[kx][k] + kb * 2;
         ptx::mma_f16_ss_acc(d1, alo, Cfg::hi(k), blo + b1, Cfg::hi(k), i1);
         if (SPLIT) ptx::mma_f16_ss_acc(d2, alo, Cfg::hi(k), blo + b2, Cfg::hi(k), i2);
@@ -635,18 +640,37 @@ __global__ void __launch_bounds__(kThreads, 1) conv3x3_tc_kernel(const __grid_co
 // WIDE (640 threads), 4..11 and 12..19 are the pipes' epilogues, warp w taking lane quarter
 // w % 4 and 32-channel group ((w - 4) / 4) % 2. The 2x DepthToSpace tail (EPI 1) is built
 // for two CTAs per SM, each with half of the TMEM columns.
+//
+// kx-in-N tail (EPI 3, M = 4 output channels before a 2x DepthToSpace): the three
+// horizontal taps move from K into N. One weight block per chunk holds, per kernel row ky,
+// the 16 columns kx * 4 + m (12 used), so an input row takes C / 16 MMAs of N = 48 instead
+// of 3 * C / 16. TMEM lane l then holds the three partial sums P_kx (bias on kx = 1) of
+// the pixel in slot row l, and an output pixel p takes P_0(p - 1) + P_1(p) + P_2(p + 1).
+// The slot holds four 32-pixel sub-tiles loaded 30 pixels apart (one TMA load each), so
+// the 32 lanes a warp may read (TMEM lane quarter q) cover pixels x0 + 30q - 1 .. +30:
+// lanes 1..30 output, their neighbours come by warp shuffle, and no warp waits for
+// another. A strip advances 120 pixels; the smaller slots (128 rows) let each pipe keep
+// three input rows in flight, which a tail with this little work per row needs to cover
+// the load latency.
 // ---------------------------------------------------------------------------
 constexpr int kThreads2 = 384;
 // Wide epilogue (SiLU NHWC layers of 64 channels, whose epilogue math is the bound): eight
 // epilogue warps per pipe, one per (TMEM lane quarter, 32-channel group).
 constexpr int kThreads2W = 640;
 constexpr int kMaxEpiWarps2 = 16;
+// kx-in-N tail: pixels per sub-tile load, pixels a sub-tile advances (30 outputs per
+// warp), and pixels a strip advances.
+constexpr int kKxnSub = 32;
+constexpr int kKxnSubStep = 30;
+constexpr int kKxnStride = 4 * kKxnSubStep;
 
 template <int NC64, int NC32, int NC16, int EPI, int ACT, int WIDE>
-__global__ void __launch_bounds__(WIDE ? kThreads2W : kThreads2, EPI == 1 ? 2 : 1)
+__global__ void __launch_bounds__(WIDE ? kThreads2W : kThreads2, (EPI == 1 || EPI == 3) ? 2 : 1)
     conv3x3_tc_vert2_kernel(const __grid_constant__ ConvTcArgs a) {
   using Cfg = ChunkCfg<NC64, NC32, NC16>;
   static_assert(!WIDE || EPI == 0, "the wide epilogue is for NHWC outputs");
+  constexpr int kStride = EPI == 3 ? kKxnStride : kTcTilePx;  // pixels a strip advances
+  constexpr int NKX = EPI == 3 ? 1 : 3;                        // weight blocks (kx) per chunk
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sW = smem;
@@ -713,7 +737,13 @@ __global__ void __launch_bounds__(WIDE ? kThreads2W : kThreads2, EPI == 1 ? 2 : 
     uint4* row = reinterpret_cast<uint4*>(sBiasB + r * 32);
     row[0] = make_uint4(0, 0, 0, 0);
     row[1] = make_uint4(0, 0, 0, 0);
-    *reinterpret_cast<__half*>(sBiasB + swz_granule(r, 0, 32)) = __float2half(a.bias[m0 + r]);
+    float bv = 0.f;
+    if constexpr (EPI == 3) {  // columns kx * M + m: the bias goes with the centre tap kx = 1
+      if (r >= a.M && r < 2 * a.M) bv = a.bias[r - a.M];
+    } else {
+      bv = a.bias[m0 + r];
+    }
+    *reinterpret_cast<__half*>(sBiasB + swz_granule(r, 0, 32)) = __float2half(bv);
   }
   ptx::fence_proxy_async_smem();  // the tensor core reads the generic writes above
   ptx::tc_fence_before();
@@ -731,8 +761,9 @@ __global__ void __launch_bounds__(WIDE ? kThreads2W : kThreads2, EPI == 1 ? 2 : 
     const int pp = warp == 0 ? 0 : 1;
     if (lane == 0) {
       if (pp == 0) {
-        // weight blocks: 3 kx x chunks of 3M rows (the three ky stacked)
-        constexpr int nblk = 3 * Cfg::N;
+        // weight blocks: 3 kx x chunks of 3M rows (the three ky stacked); EPI 3: one block
+        // per chunk
+        constexpr int nblk = NKX * Cfg::N;
         const int wrows = 3 * a.MT;
         uint32_t wbytes = 0;
 #pragma unroll
@@ -756,7 +787,7 @@ __global__ void __launch_bounds__(WIDE ? kThreads2W : kThreads2, EPI == 1 ? 2 : 
       Segment sg;
       bool ok = true;
       while (ok && it.next(sg)) {
-        const int x0 = sg.strip * kTcTilePx - 1;
+        const int x0 = sg.strip * kStride - 1;
         for (int r = sg.ya - 1; r <= sg.yb; ++r, ++g, rp.step(S)) {
           const uint32_t slot = rp.slot;
           if (!ptx::mbar_wait(ptx::smem_u32(&pempty[slot]), rp.phase ^ 1u, abort_flag, a.wait_limit_ns)) {
@@ -767,8 +798,17 @@ __global__ void __launch_bounds__(WIDE ? kThreads2W : kThreads2, EPI == 1 ? 2 : 
           ptx::mbar_arrive_expect_tx(fb, a.slot_tx);
           if (static_cast<int>(g) == a.stall_row) continue;  // failure-path test: never completes
           const uint32_t dst = ptx::smem_u32(pA + slot * a.slot_bytes);
+          if constexpr (EPI == 3) {
 #pragma unroll
-          for (int k = 0; k < Cfg::N; ++k) ptx::tma_load_3d(dst + Cfg::off(k), &a.maps[k], fb, a.c0[k], x0, r);
+            for (int k = 0; k < Cfg::N; ++k)
+#pragma unroll
+              for (int sq = 0; sq < 4; ++sq)
+                ptx::tma_load_3d(dst + Cfg::off128(k) + sq * kKxnSub * Cfg::rb(k), &a.maps[k], fb, a.c0[k],
+                                 x0 + sq * kKxnSubStep, r);
+          } else {
+#pragma unroll
+            for (int k = 0; k < Cfg::N; ++k) ptx::tma_load_3d(dst + Cfg::off(k), &a.maps[k], fb, a.c0[k], x0, r);
+          }
         }
       }
       // Never leave a TMA write in flight at exit: wait (time-bounded) for the last loads.
@@ -801,7 +841,7 @@ __global__ void __launch_bounds__(WIDE ? kThreads2W : kThreads2, EPI == 1 ? 2 : 
 #pragma unroll
       for (int kx = 0; kx < 3; ++kx)
 #pragma unroll
-        for (int k = 0; k < Cfg::N; ++k) bv[kx][k] = ptx::desc_lo(sW_u + a.wofs[kx * Cfg::N + k]);
+        for (int k = 0; k < Cfg::N; ++k) bv[kx][k] = kx < NKX ? ptx::desc_lo(sW_u + a.wofs[kx * Cfg::N + k]) : 0u;
       bool ok = ptx::mbar_wait(ptx::smem_u32(wbar), 0, abort_flag, a.wait_limit_ns);
       SegIter it{pp == 0 ? t0 : tm, pp == 0 ? tm : t1, a.H};
       Segment sg;
@@ -833,9 +873,9 @@ __global__ void __launch_bounds__(WIDE ? kThreads2W : kThreads2, EPI == 1 ? 2 : 
           const uint32_t sl = alo0 + slot * slot16;
           // One branch per row, none per MMA.
           if (n2 == 0) {
-            vert_row_mmas<Cfg, false>(sl, bv, M, ky_lo, n1, d1, d2, i1, i2);
+            vert_row_mmas<Cfg, false, NKX>(sl, bv, M, ky_lo, n1, d1, d2, i1, i2);
           } else {
-            vert_row_mmas<Cfg, true>(sl, bv, M, ky_lo, n1, d1, d2, i1, i2);
+            vert_row_mmas<Cfg, true, NKX>(sl, bv, M, ky_lo, n1, d1, d2, i1, i2);
           }
           ptx::mma_commit(ptx::smem_u32(&pempty[slot]));
           if (ky_hi == 2) {  // output row j-2 received its last kernel row
@@ -857,7 +897,8 @@ __global__ void __launch_bounds__(WIDE ? kThreads2W : kThreads2, EPI == 1 ? 2 : 
     const int e = warp - 4;
     const int pp = WIDE ? (e >> 3) : (e >> 2);    // pipe
     const int q = warp & 3;                       // tensor-memory lane quarter this warp may access
-    constexpr int KG = WIDE ? 1 : 2;              // 32-channel groups of this warp
+    // 32-channel groups of this warp (the DepthToSpace tails have M <= 16: one)
+    constexpr int KG = (WIDE || EPI == 1 || EPI == 3) ? 1 : 2;
     const int gsel = WIDE ? ((e >> 2) & 1) : 0;   // its first group
     const int ngroups = (a.MT + 31) / 32;
     const int act = ACT >= 0 ? ACT : a.act;
@@ -893,9 +934,10 @@ __global__ void __launch_bounds__(WIDE ? kThreads2W : kThreads2, EPI == 1 ? 2 : 
       }
     };
     while (ok && it.next(sg)) {
-      const int xw = sg.strip * kTcTilePx + q * 32;  // first pixel of this warp's 32
+      // first pixel of this warp's 32 (EPI 3: sub-tile q, from one pixel left of its outputs)
+      const int xw = EPI == 3 ? sg.strip * kStride - 1 + q * kKxnSubStep : sg.strip * kTcTilePx + q * 32;
       const int x = xw + lane;
-      const bool valid = x < a.W;
+      const bool valid = EPI == 3 ? (lane >= 1 && lane <= kKxnSubStep && x < a.W) : x < a.W;
       const bool wl = xw < a.W;  // this warp stores anything in this strip
       for (int y = sg.ya; y < sg.yb; ++y) {
         // accumulator of this output row: consecutive rows sit in descending chunks
@@ -1016,6 +1058,17 @@ __global__ void __launch_bounds__(WIDE ? kThreads2W : kThreads2, EPI == 1 ? 2 : 
               }
               *sp = make_uint4(h[0], h[1], h[2], h[3]);
             }
+          } else if constexpr (EPI == 3) {
+            // P_0 of the pixel on the left and P_2 of the pixel on the right (accumulator
+            // columns kx * 4 + m), from the neighbouring lanes of this warp
+            uint32_t ov[32];
+#pragma unroll
+            for (int m = 0; m < 4; ++m) {
+              const float l = __shfl_up_sync(0xffffffffu, __uint_as_float(rr[m]), 1);
+              const float r = __shfl_down_sync(0xffffffffu, __uint_as_float(rr[8 + m]), 1);
+              ov[m] = __float_as_uint(l + __uint_as_float(rr[4 + m]) + r);
+            }
+            if (valid) store_dts2_nchw<1>(ov, act, o, y, x, a.H, a.W);
           } else if constexpr (EPI == 1) {
             if (valid) {
               switch (a.M >> 2) {
@@ -1108,6 +1161,7 @@ KernelFn pick(bool vert, int variant) {
       case 2: return conv3x3_tc_vert2_kernel<NC64, NC32, NC16, 0, kActSilu, 0>;
       case 3: return conv3x3_tc_vert2_kernel<NC64, NC32, NC16, 1, -1, 0>;
       case 4: return conv3x3_tc_vert2_kernel<NC64, NC32, NC16, 2, -1, 0>;
+      case 6: return conv3x3_tc_vert2_kernel<NC64, NC32, NC16, 3, -1, 0>;
       default: return conv3x3_tc_vert2_kernel<NC64, NC32, NC16, 0, kActSilu, 1>;
     }
   }

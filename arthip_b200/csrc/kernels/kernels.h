@@ -53,6 +53,10 @@ struct ConvTcWeights {
   // Mpad rows per (tap, chunk).
   int vert = 0;
   int vmt = 0;
+  // kx-in-N tail blocks (M == 4, vertical window): one block per chunk after the blocks
+  // above, rows ky * 16 + kx * 4 + m (12 of each 16 used), for the 2x DepthToSpace tail.
+  int kxn = 0;
+  long long kxn_gofs[kTcMaxChunks] = {};
   int nchunks = 0;
   ConvTcChunk chunk[kTcMaxChunks];
   void* wpack = nullptr;       // device: swizzled K-major weight blocks (see vert)
@@ -73,6 +77,9 @@ struct ConvTcOut {
   int fp32 = 0;
   int clip = 0;
   float clip_lo = 0.f, clip_hi = 0.f;
+  // Residual operands the launches of this plan pass (-1: not known). A 2x DepthToSpace
+  // tail of four channels without any takes the kx-in-N form.
+  int adds = -1;
 };
 
 // Per (layer, buffers, frame size) launch plan.
@@ -88,6 +95,7 @@ struct ConvTcPlan {
   size_t smem_bytes = 0;
   int nacc = 0, acc_stride = 0, tmem_cols = 0;
   int vert = 0;                // vertical window (two row pipelines per CTA; weights packed accordingly)
+  int kxn = 0;                 // the kx-in-N 2x DepthToSpace tail (strips of 126 pixels)
   int grid_x = 0;
   ConvTcOut out;
   CUtensorMap maps[kTcMaxChunks];
