@@ -270,7 +270,7 @@ cudaError_t simt_conv_upload(const uint16_t* w_oihw, const float* bias, int C, i
   if (e != cudaSuccess) return e;
   e = cudaMemcpy(out->bias, b.data(), sizeof(float) * M, cudaMemcpyHostToDevice);
   if (e != cudaSuccess || !head_mma_supported(C, M)) return e;
-  const std::vector<uint32_t> f = head_mma_fragments(w_oihw, C, M);
+  const std::vector<uint32_t> f = head_mma_fragments(w_oihw, bias, C, M);
   e = cudaMalloc(&out->bfrag, f.size() * sizeof(uint32_t));
   if (e != cudaSuccess) return e;
   return cudaMemcpy(out->bfrag, f.data(), f.size() * sizeof(uint32_t), cudaMemcpyHostToDevice);

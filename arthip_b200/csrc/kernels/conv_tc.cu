@@ -85,6 +85,16 @@ bool encode(EncodeTiledFn enc, CUtensorMap* map, const void* base, int C, int W,
 
 }  // namespace
 
+bool encode_nhwc_map(CUtensorMap* map, const void* base, int C, int W, int H, int box_c, int box_px,
+                     std::string* err) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (!enc) {
+    if (err) *err = "cuTensorMapEncodeTiled is unavailable from the CUDA driver";
+    return false;
+  }
+  return encode(enc, map, base, C, W, H, box_c, box_px, err);
+}
+
 bool conv_tc_supported(int C, int M, std::string* why) {
   // Three input-row slots of C channels plus the weights must fit in shared memory:
   // up to two 64-channel chunks per pixel row.

@@ -102,6 +102,10 @@ struct ConvTcPlan {
   CUtensorMap out_map32, out_map16;
 };
 
+// Tensor map over an NHWC fp16 tensor [H][W][C] with a {box_c, box_px, 1} box, swizzled to
+// match a box_c * 2-byte row (box_c 64: 128B, 32: 64B, 16: 32B swizzle).
+bool encode_nhwc_map(CUtensorMap* map, const void* base, int C, int W, int H, int box_c, int box_px,
+                     std::string* err);
 // Returns true when the tensor-core kernel covers (C, M); otherwise fills `why`.
 bool conv_tc_supported(int C, int M, std::string* why);
 // Packs fp16 weights OIHW [M][C][3][3] (host, as fp16 bits) and fp32 bias into device memory.
@@ -205,7 +209,8 @@ cudaError_t simt_conv_launch(const SimtConvWeights& w, const __half* in, int H, 
 // plain NHWC fp16 output without residual adds (conv_head.cu). simt_conv_upload /
 // simt_conv_launch use it when it applies.
 bool head_mma_supported(int C, int M);
-std::vector<uint32_t> head_mma_fragments(const uint16_t* w_oihw_f16, int C, int M);
+// (C == 1: the bias rides in the fragments, as the product of a constant 1 in K slot 12)
+std::vector<uint32_t> head_mma_fragments(const uint16_t* w_oihw_f16, const float* bias_or_null, int C, int M);
 cudaError_t head_mma_launch(const uint32_t* bfrag, const float* bias, int C, int M, const __half* in, int H, int W,
                             int act, __half* out, cudaStream_t s);
 
