@@ -46,6 +46,13 @@ CUtensorMapSwizzle swizzle_for(int cw) {
 }
 int round_up(int v, int a) { return (v + a - 1) / a * a; }
 
+// kx-in-N tail: two CTAs per SM (four row pipelines), two input slots per pipeline. Measured
+// on B200 (R8F64 tail, 1080p, CUDA events in the frame graph): 2 slots 0.0607 ms, 3 slots
+// 0.0624 ms, one CTA per SM with 6 slots per pipeline 0.0646 ms; deeper rings do not help
+// a tail whose rows are bound by their per-row MMA and epilogue chains.
+constexpr bool kKxnTwoCtas = true;
+constexpr int kKxnMaxSlots = 2;
+
 void make_chunks(int C, ConvTcWeights* w) {
   int c = 0, n = 0;
   while (c < C) {
@@ -285,8 +292,7 @@ bool conv_tc_plan(const ConvTcWeights* w, const __half* in, int H, int W, const 
       slots = 2;
       // The kx-in-N form of the tail, for a launch without residual operands
       // (ARTHIP_TAIL_KXN=0 keeps the three-kx form; read when the plan is built, never at
-      // launch). Its slots are 128 rows, its weights one block per chunk: as many slots
-      // as fit in half of the SM's shared memory.
+      // launch). Its slots are 128 rows, its weights one block per chunk.
       const char* v = std::getenv("ARTHIP_TAIL_KXN");
       if (w->kxn && out.adds == 0 && !(v && *v == '0')) {
         int kslot = 0, kw = 0;
@@ -294,14 +300,15 @@ bool conv_tc_plan(const ConvTcWeights* w, const __half* in, int H, int W, const 
           kslot += kTcTilePx * w->chunk[k].rowbytes;
           kw += round_up(3 * w->vmt * w->chunk[k].rowbytes, 1024);
         }
+        const int limit = kKxnTwoCtas ? kSmemPerSm / 2 - 1024 : kSmemLimit;
         int ks = 0;
-        for (int s2 = kMaxSlots; s2 >= 2 && !ks; --s2)
-          if (kw + 2 * s2 * kslot + 4096 + round_up(w->vmt * 32, 1024) + kTailBytes + 1024 <= kSmemPerSm / 2 - 1024)
-            ks = s2;
+        for (int s2 = kKxnMaxSlots; s2 >= 2 && !ks; --s2)
+          if (kw + 2 * s2 * kslot + 4096 + round_up(w->vmt * 32, 1024) + kTailBytes + 1024 <= limit) ks = s2;
         if (ks) {
           P->kxn = 1;
           slots = ks;
           P->slot_bytes = kslot;
+          dual = kKxnTwoCtas;
         }
       }
     }

@@ -649,9 +649,7 @@ __global__ void __launch_bounds__(kThreads, 1) conv3x3_tc_kernel(const __grid_co
 // The slot holds four 32-pixel sub-tiles loaded 30 pixels apart (one TMA load each), so
 // the 32 lanes a warp may read (TMEM lane quarter q) cover pixels x0 + 30q - 1 .. +30:
 // lanes 1..30 output, their neighbours come by warp shuffle, and no warp waits for
-// another. A strip advances 120 pixels; the smaller slots (128 rows) let each pipe keep
-// three input rows in flight, which a tail with this little work per row needs to cover
-// the load latency.
+// another. A strip advances 120 pixels.
 // ---------------------------------------------------------------------------
 constexpr int kThreads2 = 384;
 // Wide epilogue (SiLU NHWC layers of 64 channels, whose epilogue math is the bound): eight
