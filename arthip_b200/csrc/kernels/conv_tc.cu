@@ -285,31 +285,34 @@ bool conv_tc_plan(const ConvTcWeights* w, const __half* in, int H, int W, const 
     // The 2x DepthToSpace tail (narrow N, little tensor work per row) is bound by its
     // per-row MMA issue and epilogue chains, not by loads: it runs two CTAs per SM, each
     // with two input slots per pipe and half of the tensor memory.
-    dual = out.mode == 1 && out.dts_b == 2 && (out.nchw || w->M == 4) && w->M % 4 == 0 && w->Mpad == 16 &&
-           smem_need(w, w->vmt, true, out.mode, 2) <= kSmemPerSm / 2 - 1024;
-    if (dual) {
-      chosen = w->vmt;
-      slots = 2;
-      // The kx-in-N form of the tail, for a launch without residual operands
-      // (ARTHIP_TAIL_KXN=0 keeps the three-kx form; read when the plan is built, never at
-      // launch). Its slots are 128 rows, its weights one block per chunk.
-      const char* v = std::getenv("ARTHIP_TAIL_KXN");
-      if (w->kxn && out.adds == 0 && !(v && *v == '0')) {
-        int kslot = 0, kw = 0;
-        for (int k = 0; k < w->nchunks; ++k) {
-          kslot += kTcTilePx * w->chunk[k].rowbytes;
-          kw += round_up(3 * w->vmt * w->chunk[k].rowbytes, 1024);
-        }
-        const int limit = kKxnTwoCtas ? kSmemPerSm / 2 - 1024 : kSmemLimit;
-        int ks = 0;
-        for (int s2 = kKxnMaxSlots; s2 >= 2 && !ks; --s2)
-          if (kw + 2 * s2 * kslot + 4096 + round_up(w->vmt * 32, 1024) + kTailBytes + 1024 <= limit) ks = s2;
-        if (ks) {
+    const bool dts_tail =
+        out.mode == 1 && out.dts_b == 2 && (out.nchw || w->M == 4) && w->M % 4 == 0 && w->Mpad == 16;
+    // The kx-in-N form of a four-channel tail, for a launch without residual operands
+    // (ARTHIP_TAIL_KXN=0 keeps the three-kx form; read when the plan is built, never at
+    // launch). Its slots are 128 rows and its weights one block per chunk, so it fits
+    // twice per SM up to C = 96.
+    const char* v = std::getenv("ARTHIP_TAIL_KXN");
+    if (dts_tail && w->kxn && out.adds == 0 && !(v && *v == '0')) {
+      int kslot = 0, kw = 0;
+      for (int k = 0; k < w->nchunks; ++k) {
+        kslot += kTcTilePx * w->chunk[k].rowbytes;
+        kw += round_up(3 * w->vmt * w->chunk[k].rowbytes, 1024);
+      }
+      const int limit = kKxnTwoCtas ? kSmemPerSm / 2 - 1024 : kSmemLimit;
+      for (int s2 = kKxnMaxSlots; s2 >= 2 && !chosen; --s2)
+        if (kw + 2 * s2 * kslot + 4096 + round_up(w->vmt * 32, 1024) + kTailBytes + 1024 <= limit) {
           P->kxn = 1;
-          slots = ks;
           P->slot_bytes = kslot;
+          chosen = w->vmt;
+          slots = s2;
           dual = kKxnTwoCtas;
         }
+    }
+    if (!chosen) {
+      dual = dts_tail && smem_need(w, w->vmt, true, out.mode, 2) <= kSmemPerSm / 2 - 1024;
+      if (dual) {
+        chosen = w->vmt;
+        slots = 2;
       }
     }
     for (int s = kMaxSlots; s >= min_slots && !chosen; --s)
