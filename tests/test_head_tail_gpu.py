@@ -115,3 +115,43 @@ def test_tail_kxn_matches_three_kx_form(tmp_path, monkeypatch, cfg, H, W):
     ulp = 2.0 ** (np.floor(np.log2(mag)) - 10)
     assert (d <= ulp + 2.0 ** -16).all(), f"{cfg}: max diff {d.max():.3g}"
     assert (d == 0).mean() > 0.99, f"{cfg}: only {(d == 0).mean():.4f} identical"
+
+
+def test_tail_timed_out_wait_is_reported_and_recovers(tmp_path, monkeypatch):
+    """Failure detection without a GPU fault, through the kx-in-N tail: a model whose only
+    tensor-core launch is the 64 -> 4 DepthToSpace tail; every pipeline arms its second
+    input row's slot without loading it, so the MMA issuer's bounded wait (shortened to
+    50 ms) runs out. The engine must report the timed-out wait, and the same engine must
+    then produce the oracle's frame, as must a new engine on the same context. The first
+    engine launches its ops one by one (`ARTHIP_NO_GRAPH=1`): a captured CUDA graph would
+    keep the launch arguments of the faulted frame."""
+    from arthip_b200.engine import EngineHarnessError
+    from arthip_b200.modelgen import _conv_node, _half, _model, kern, linspace
+    from arthip_b200.native import lib
+    C, H, W = 64, 29, 250
+    w = kern(7, 4, C) * 0.25
+    b = linspace(4, -0.05, 0.05)
+    nodes = [_conv_node("x", "w", "b", "raw"),
+             op.make_node("DepthToSpace", ["raw"], ["y"], blocksize=2, mode="DCR")]
+    model = _model(nodes, "x", [1, C, "h", "w"], op.FLOAT16, "y", [1, 1, "2*h", "2*w"], op.FLOAT16,
+                   [_half("w", w), _half("b", b)])
+    p = tmp_path / "tail_only.onnx"
+    op.save_model(model, p)
+    x = modelgen.synthetic_frame(3, C, H, W)
+    monkeypatch.setenv("ARTHIP_NO_GRAPH", "1")
+    eng = Engine(p)
+    monkeypatch.delenv("ARTHIP_NO_GRAPH")
+    lib().ah_test_set_conv_fault_hook(50, 1)
+    try:
+        with pytest.raises(EngineHarnessError, match="timed-out"):
+            eng.run(x)
+    finally:
+        lib().ah_test_set_conv_fault_hook(0, -1)
+    got = eng.run(x).astype(np.float64)
+    xd = x.astype(np.float64)
+    ref16 = onnx_cpu.run_model(model, xd, mode="fp16_nodes")
+    ref32 = onnx_cpu.run_model(model, xd, mode="fp32_nodes")
+    variants = [onnx_cpu.run_model(model, xd, mode="fp16_nodes", use_torch=False)]
+    check_against_oracles(got, ref16, ref32, variants, "tail only, after recovery")
+    again = Engine(p).run(x).astype(np.float64)
+    assert np.array_equal(again, got), "a new engine (CUDA graph) differs from the recovered one"
