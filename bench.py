@@ -445,6 +445,10 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--e2e-steps", type=int, default=None)
     ap.add_argument("--e2e-engines", type=int, default=2)
+    ap.add_argument("--streams", type=int, default=2,
+                    help="device-resident line: frames round-robin over this many engines, each on its own "
+                         "stream, so one frame's kernels can start on SMs another frame's kernels free "
+                         "(the reference's filter runs num_streams engines the same way)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--config", default="C2", choices=sorted(CONFIG_TABLE),
                     help="C2 (default): R8F64 1080p; C3: R16F96 1080p; C4: R8F64 2160p; ArtCNN: the "
@@ -481,48 +485,62 @@ def main():
 
     with tempfile.TemporaryDirectory() as td:
         cm, path = build_model(Path(td))
-        eng = Engine(path, device=local)
-        in_ptr, out_ptr, in_bytes, out_bytes = eng.prepare(1, H, W)
+        n_str = max(1, args.streams)
+        teng = [Engine(path, device=local) for _ in range(n_str)]  # timed engines, one stream each
+        eng = teng[0]
+        preps = [e.prepare(1, H, W) for e in teng]
+        in_ptr, out_ptr, in_bytes, out_bytes = preps[0]
         ops = eng.ops()
 
         # input ring: 8 distinct synthetic frames resident in HBM
         ring = torch.stack([torch.from_numpy(modelgen.synthetic_frame(sd, 1, H, W).reshape(-1))
                             for sd in frame_seeds(rank, 8)]).to(dev)
         torch.cuda.synchronize()
-        estream = torch.cuda.ExternalStream(eng.stream, device=dev)
+        estreams = [torch.cuda.ExternalStream(e.stream, device=dev) for e in teng]
+        estream = estreams[0]
 
-        def in_view():
+        def in_view(ptr):
             class _B:
-                __cuda_array_interface__ = {"shape": (in_bytes // 2,), "typestr": "<f2", "data": (in_ptr, False),
+                __cuda_array_interface__ = {"shape": (in_bytes // 2,), "typestr": "<f2", "data": (ptr, False),
                                             "version": 3}
             return torch.as_tensor(_B(), device=dev)
-        dst = in_view()
+        dsts = [in_view(pr[0]) for pr in preps]
 
-        def step(i):
-            with torch.cuda.stream(estream):
-                dst.copy_(ring[i % 8], non_blocking=True)
-            eng.enqueue()
+        def step(i, k=None):
+            # frame i on engine i % n_str (k forces one engine: the per-op pass)
+            k = i % n_str if k is None else k
+            with torch.cuda.stream(estreams[k]):
+                dsts[k].copy_(ring[i % 8], non_blocking=True)
+            teng[k].enqueue()
 
         # the clock sampler starts before the warm-up so that its first sample is out by
         # the time the timed region begins
         clk = ClockSampler(_gpu_uuid(dev)).start()
         try:
-            for i in range(args.warmup):
+            for i in range(max(args.warmup, n_str)):
                 step(i)
-            eng.synchronize()
+            for e in teng:
+                e.synchronize()
             clk.wait_first()
 
-            # -------- timed region: K frames through the captured CUDA graph --------
+            # -------- timed region: K frames through the captured CUDA graph(s) --------
             dist_barrier(world)
             torch.cuda.synchronize()
             ev0 = torch.cuda.Event(enable_timing=True)
             ev1 = torch.cuda.Event(enable_timing=True)
             with clk.window():
                 ev0.record(estream)
+                for st_ in estreams[1:]:
+                    st_.wait_event(ev0)  # no engine starts before the region opens
                 for i in range(args.steps):
                     step(i)
+                for st_ in estreams[1:]:  # the region closes when every engine's last frame is done
+                    done = torch.cuda.Event()
+                    done.record(st_)
+                    estream.wait_event(done)
                 ev1.record(estream)
-                eng.synchronize()
+                for e in teng:
+                    e.synchronize()
                 torch.cuda.synchronize()
         finally:
             clk.stop()
@@ -535,7 +553,7 @@ def main():
         op_frames = max(3, min(args.steps, 50))
         eng.timing_start(op_frames)
         for i in range(op_frames):
-            step(i)
+            step(i, 0)
         op_ms, _, op_count = eng.timing_read()
         op_ms = [t / op_count for t in op_ms]
 
@@ -648,7 +666,8 @@ def main():
         "dtype": "fp16", "data": "synthetic",
         "config": {"workload": WORKLOAD, "frames_per_gpu": frames, "input_ring": 8,
                    "l2": "activations (265 MB/tensor) exceed the 126 MB L2; no flush",
-                   "parallelism": f"frame-parallel x{world}, no collectives"},
+                   "parallelism": f"frame-parallel x{world}, no collectives",
+                   "streams_per_gpu": n_str},
         "clocks": {"sm_mhz": clocks["sm_mhz"], "sm_max_mhz": clocks["sm_max_mhz"], "reasons": clocks["reasons"],
                    "samples": clocks["samples"]},
         "e2e": {"value": world * e2e_steps / e2e_s, "unit": UNIT, "h2d_bytes_per_step": in_bytes,
